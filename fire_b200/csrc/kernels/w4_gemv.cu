@@ -1,0 +1,280 @@
+// INT4 group-128 GEMV for single-token decode (M = 1) on sm_100a.
+//
+// Replaces Fire's GEMV_int4_v1 / matmul_quant_kernel_cu
+// (src/op/kernels/cuda/matmul_kernel.cu:230-314) for the .fire v2 layout:
+//   qweight u8 [N, K/2] (even k in the low nibble), scales f32 [N, K/128],
+//   zero points u8 [N, K/128], x f32 [K], y f32 [N],
+//   y[n] = sum_k x[k] * (q[n,k] - z[n,g]) * s[n,g],  g = k / 128.
+//
+// Design (HBM-bound: 0.539 B per weight, the kernel must issue < ~2.2 ops/weight):
+//  * Each lane streams 16-byte chunks (32 nibbles, always inside one group) with
+//    L1-bypassing 128-bit loads; a warp owns a tile of R rows, so every x value read
+//    from shared memory is reused R times.
+//  * Dequantisation is integer-free: (w & (0xF << 4j)) | 0x4B000000 is the float
+//    2^23 + q*16^j exactly (j <= 4; nibbles 5..7 are shifted down by 12 bits first),
+//    and one packed FP32 add of -(2^23 + z*16^j) leaves (q - z)*16^j exactly. x is
+//    staged pre-multiplied by 16^-j, so each packed FMA accumulates x*(q-z) exactly as
+//    rounded products; the group scale multiplies each 32-value partial sum.
+//  * __fadd2_rn/__ffma2_rn (sm_100 packed FP32) do two weights per instruction.
+//  * x is staged once per CTA in shared memory, transposed ([8][K/32] float4) so that
+//    lanes reading consecutive chunks hit consecutive 16-byte words (no bank conflicts).
+//  * Optional RMSNorm prologue (the norm feeding q/k/v and gate/up), residual-add
+//    epilogue (o/down) and SwiGLU epilogue (gate/up packed per tile), so the decode
+//    layer needs no separate norm/add/swiglu launches.
+//  * Programmatic dependent launch: weight prefetch to L2 is issued before waiting on
+//    the producer of x.
+#include "common.cuh"
+#include "w4_gemv.h"
+
+namespace fb {
+
+namespace {
+
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr uint32_t kMagic = 0x4B000000u;  // float 2^23
+
+__device__ __forceinline__ float2 magic2(uint32_t a, uint32_t b) {
+    return make_float2(__uint_as_float(a | kMagic), __uint_as_float(b | kMagic));
+}
+
+// sum over the 32 weights of one 16-byte chunk of x'[k] * (q[k]-z)*16^p(k)
+// where x' = x * 16^-p(k) (pre-scaled in shared memory).
+__device__ __forceinline__ float chunk_dot(const uint4 w, const uint32_t z, const float4* xv) {
+    const float2 n01 = make_float2(-__uint_as_float(kMagic | z), -__uint_as_float(kMagic | (z << 4)));
+    const float2 n23 = make_float2(-__uint_as_float(kMagic | (z << 8)),
+                                   -__uint_as_float(kMagic | (z << 12)));
+    const float2 n42 = make_float2(-__uint_as_float(kMagic | (z << 16)), n23.x);
+    const float2 n34 = make_float2(n23.y, n42.x);
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const uint32_t v = ws[m], t = v >> 12;
+        const float2 d01 = __fadd2_rn(magic2(v & 0xFu, v & 0xF0u), n01);
+        const float2 d23 = __fadd2_rn(magic2(v & 0xF00u, v & 0xF000u), n23);
+        const float2 d45 = __fadd2_rn(magic2(v & 0xF0000u, t & 0xF00u), n42);
+        const float2 d67 = __fadd2_rn(magic2(t & 0xF000u, t & 0xF0000u), n34);
+        const float4 xa = xv[2 * m], xb = xv[2 * m + 1];
+        acc0 = __ffma2_rn(make_float2(xa.x, xa.y), d01, acc0);
+        acc1 = __ffma2_rn(make_float2(xa.z, xa.w), d23, acc1);
+        acc0 = __ffma2_rn(make_float2(xb.x, xb.y), d45, acc0);
+        acc1 = __ffma2_rn(make_float2(xb.z, xb.w), d67, acc1);
+    }
+    return (acc0.x + acc1.x) + (acc0.y + acc1.y);
+}
+
+// Stage x (optionally RMS-normalised) into xs[i][c], scaled by 16^-p.
+__device__ __forceinline__ void stage_x(const W4Args& a, float4* xs, float* red) {
+    const int K = a.K, chunks = K >> 5;
+    float scale = 1.0f;
+    if (a.norm_w != nullptr) {
+        float ss = 0.0f;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            const float v = a.x[k];
+            ss = fmaf(v, v, ss);
+        }
+        ss = block_sum(ss, red);
+        scale = 1.0f / sqrtf(ss / static_cast<float>(K) + a.eps);
+    }
+    for (int k4 = threadIdx.x; k4 < (K >> 2); k4 += blockDim.x) {
+        float4 v = make_float4(a.x[4 * k4], a.x[4 * k4 + 1], a.x[4 * k4 + 2], a.x[4 * k4 + 3]);
+        if (a.norm_w != nullptr) {
+            const float* w = a.norm_w + 4 * k4;
+            v = make_float4(v.x * w[0] * scale, v.y * w[1] * scale, v.z * w[2] * scale,
+                            v.w * w[3] * scale);
+        }
+        const int i = k4 & 7, c = k4 >> 3;
+        if ((i & 1) == 0) {
+            v.y *= 0.0625f;
+            v.z *= 0.00390625f;
+            v.w *= 0.000244140625f;
+        } else {
+            v.x *= 1.52587890625e-05f;
+            v.y *= 0.00390625f;
+            v.z *= 0.000244140625f;
+            v.w *= 1.52587890625e-05f;
+        }
+        xs[i * chunks + c] = v;
+    }
+}
+
+template <int R, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) w4g128_gemv_kernel(const W4Args a) {
+    extern __shared__ float4 xs[];
+    __shared__ float red[32];
+    const int K = a.K, N = a.N;
+    const int chunks = K >> 5, groups = K >> 7;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tiles = (N + R - 1) / R;
+    const size_t row_bytes = static_cast<size_t>(K) >> 1;
+
+    // Weights never depend on the previous kernel: start pulling this CTA's first
+    // tiles into L2 before waiting for x.
+    if (a.prefetch && lane == 0) {
+        const int t = blockIdx.x + gridDim.x * warp;
+        if (t < tiles) {
+            const int rows = min(R, N - t * R);
+            prefetch_l2_bulk(a.qw + static_cast<size_t>(t) * R * row_bytes,
+                             static_cast<uint32_t>(rows * row_bytes));
+        }
+    }
+    pdl_wait();
+    stage_x(a, xs, red);
+    __syncthreads();
+    pdl_launch_dependents();
+
+    for (int t = blockIdx.x + gridDim.x * warp; t < tiles; t += gridDim.x * kWarps) {
+        const int row0 = t * R;
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+
+        for (int c0 = lane; c0 < chunks; c0 += 64) {
+            const int c1 = c0 + 32;
+            const bool has1 = c1 < chunks;
+            uint4 w0[R], w1[R];
+            float s0[R], s1[R];
+            uint32_t z0[R], z1[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int row = min(row0 + r, N - 1);
+                const uint8_t* qrow = a.qw + static_cast<size_t>(row) * row_bytes;
+                const size_t mrow = static_cast<size_t>(row) * groups;
+                w0[r] = ldg_stream(qrow + static_cast<size_t>(c0) * 16);
+                s0[r] = __ldg(a.scales + mrow + (c0 >> 2));
+                z0[r] = __ldg(a.zeros + mrow + (c0 >> 2));
+                if (has1) {
+                    w1[r] = ldg_stream(qrow + static_cast<size_t>(c1) * 16);
+                    s1[r] = __ldg(a.scales + mrow + (c1 >> 2));
+                    z1[r] = __ldg(a.zeros + mrow + (c1 >> 2));
+                }
+            }
+            float4 xv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] = xs[i * chunks + c0];
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] = fmaf(s0[r], chunk_dot(w0[r], z0[r], xv), acc[r]);
+            if (has1) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) xv[i] = xs[i * chunks + c1];
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    acc[r] = fmaf(s1[r], chunk_dot(w1[r], z1[r], xv), acc[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+
+        if constexpr (EPI == kW4Swiglu) {
+            // Tile = R/2 gate rows then the matching R/2 up rows (packed at load time).
+            // silu(g) * u as in src/op/kernels/cuda/swiglu_kernel.cu:11-12.
+            if (lane < R / 2) {
+                float g = acc[0], u = acc[R / 2];
+#pragma unroll
+                for (int j = 1; j < R / 2; ++j)
+                    if (lane == j) { g = acc[j]; u = acc[R / 2 + j]; }
+                const float silu = g * 1.0f / (1.0f + expf(-g));
+                a.y[t * (R / 2) + lane] = silu * u;
+            }
+        } else {
+            if (lane < R) {
+                float v = acc[0];
+#pragma unroll
+                for (int j = 1; j < R; ++j)
+                    if (lane == j) v = acc[j];
+                const int row = row0 + lane;
+                if (row < N) {
+                    if constexpr (EPI == kW4Residual) v = a.residual[row] + v;
+                    a.y[row] = v;
+                }
+            }
+        }
+    }
+}
+
+template <int R, int EPI>
+cudaError_t launch_t(const W4Args& a, int num_sms, cudaStream_t stream, bool pdl) {
+    auto kern = w4g128_gemv_kernel<R, EPI>;
+    const int smem = a.K * 4;
+    if (smem > 48 * 1024) {
+        // Opt in once per device to the larger dynamic shared memory this K needs.
+        static int configured[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64 || smem > configured[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(
+                kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) configured[dev] = 227 * 1024;
+        }
+    }
+    const int tiles = (a.N + R - 1) / R;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles < num_sms ? tiles : num_sms));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+}  // namespace
+
+cudaError_t w4g128_gemv_launch(const W4Args& a, int epi, int num_sms, cudaStream_t stream,
+                               bool pdl) {
+    switch (epi) {
+    case kW4Residual: return launch_t<kW4TileRows, kW4Residual>(a, num_sms, stream, pdl);
+    case kW4Swiglu: return launch_t<kW4TileRows, kW4Swiglu>(a, num_sms, stream, pdl);
+    default: return launch_t<kW4TileRows, kW4Store>(a, num_sms, stream, pdl);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Generic path: any group size, any byte alignment, any number of input rows.
+// Same formula as matmul_quant_int4_fp32_naive (matmul_kernel.cu:202-227); one warp
+// per output element, lanes stride over k, FP32 accumulation.
+__global__ void w4_linear_generic_kernel(const float* __restrict__ x,
+                                         const uint8_t* __restrict__ qw,
+                                         const float* __restrict__ scales,
+                                         const uint8_t* __restrict__ zeros, float* __restrict__ y,
+                                         int rows, int N, int K, int group) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+    const long long total = static_cast<long long>(rows) * N;
+    const int groups = K / group;
+    for (long long o = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         o < total; o += warps) {
+        const int m = static_cast<int>(o / N), n = static_cast<int>(o % N);
+        const uint8_t* qrow = qw + static_cast<size_t>(n) * (K / 2);
+        const float* xr = x + static_cast<size_t>(m) * K;
+        float sum = 0.0f;
+        for (int k = lane; k < K; k += 32) {
+            const uint8_t b = qrow[k >> 1];
+            const int q = (k & 1) ? (b >> 4) : (b & 15);
+            const size_t gi = static_cast<size_t>(n) * groups + k / group;
+            sum = fmaf(xr[k], static_cast<float>(q - static_cast<int>(zeros[gi])) * scales[gi],
+                       sum);
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) y[static_cast<size_t>(m) * N + n] = sum;
+    }
+}
+
+cudaError_t w4_linear_generic_launch(const float* x, const uint8_t* qw, const float* scales,
+                                     const uint8_t* zeros, float* y, int rows, int N, int K,
+                                     int group, int num_sms, cudaStream_t stream) {
+    const long long warps_needed = static_cast<long long>(rows) * N;
+    long long blocks = (warps_needed + 7) / 8;
+    const long long cap = static_cast<long long>(num_sms) * 8;
+    if (blocks > cap) blocks = cap;
+    w4_linear_generic_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        x, qw, scales, zeros, y, rows, N, K, group);
+    return cudaGetLastError();
+}
+
+}  // namespace fb
