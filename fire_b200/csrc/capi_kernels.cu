@@ -47,7 +47,8 @@ int fire_b200_linear_w4(const float* x, const uint8_t* qweight, const float* sca
     if (!aligned(x, 4) || !aligned(scales, 4) || !aligned(y, 4)) return FIRE_B200_ERR_INVALID;
     int sms = 0;
     if (int e = fb::device_sms(&sms)) return e;
-    if (rows == 1 && group_size == 128 && k % 128 == 0 && aligned(qweight, 16)) {
+    // The streaming kernels stage x (k floats) in shared memory: k <= 53248 (208 KiB).
+    if (rows == 1 && group_size == 128 && k % 128 == 0 && k <= 53248 && aligned(qweight, 16)) {
         fb::W4Args a{};
         a.x = x;
         a.qw = qweight;
@@ -71,7 +72,7 @@ int fire_b200_linear_dense(const float* x, const void* weight, int weight_dtype,
     int sms = 0;
     if (int e = fb::device_sms(&sms)) return e;
     const bool bf16 = weight_dtype == FIRE_B200_BF16;
-    if (rows == 1 && k % 8 == 0 && aligned(weight, 16)) {
+    if (rows == 1 && k % 8 == 0 && k <= 53248 && aligned(weight, 16)) {
         fb::DenseArgs a{};
         a.x = x;
         a.w = weight;
@@ -128,6 +129,10 @@ int fire_b200_mha_decode(const float* q, const float* key_cache, const float* va
         return FIRE_B200_ERR_INVALID;
     if (layer < 0 || layer >= layers || pos < 0 || pos >= capacity) return FIRE_B200_ERR_INVALID;
     const size_t need = fb::attention_workspace_bytes(q_heads, kv_heads, head_dim, capacity);
+    const int group = q_heads / kv_heads, chunks = (capacity + fb::kAttnChunk - 1) / fb::kAttnChunk;
+    const size_t smem = (static_cast<size_t>(group) * (head_dim + fb::kAttnChunk + 2 + chunks) +
+                         static_cast<size_t>(fb::kAttnChunk) * (head_dim + 1)) * sizeof(float);
+    if (smem > 227 * 1024) return FIRE_B200_ERR_UNSUPPORTED;
     if (workspace_bytes < need || !aligned(workspace, 16)) return FIRE_B200_ERR_INVALID;
     const int max_chunks = (capacity + fb::kAttnChunk - 1) / fb::kAttnChunk;
     const size_t layer_off = static_cast<size_t>(layer) * capacity * kv_heads * head_dim;
