@@ -1,0 +1,587 @@
+#include "engine/qwen3.h"
+
+#include <cmath>
+#include <cstring>
+#include <unordered_map>
+
+#include "device_info.h"
+#include "fire_b200.h"
+#include "kernels/dense_gemv.h"
+#include "kernels/ops.h"
+#include "kernels/w4_gemv.h"
+
+namespace fb {
+
+namespace {
+
+#define FB_CK(expr)                                                 \
+    do {                                                            \
+        const cudaError_t e_ = (expr);                              \
+        if (e_ != cudaSuccess) return static_cast<int>(e_);         \
+    } while (0)
+#define FB_RC(expr)                     \
+    do {                                \
+        const int r_ = (expr);          \
+        if (r_ != 0) return r_;         \
+    } while (0)
+
+size_t esize(int dt) { return dt == kSrcF32 ? 4 : (dt == kSrcBF16 ? 2 : 1); }
+size_t pad256(size_t b) { return (b + 255) / 256 * 256; }
+
+class Sources {
+  public:
+    explicit Sources(const std::vector<TensorSrc>& v) {
+        for (const auto& t : v) m_[t.name] = &t;
+    }
+    const TensorSrc* get(const std::string& n) const {
+        auto it = m_.find(n);
+        return it == m_.end() ? nullptr : it->second;
+    }
+    bool has(const std::string& n) const { return m_.count(n) != 0; }
+
+  private:
+    std::unordered_map<std::string, const TensorSrc*> m_;
+};
+
+bool is(const TensorSrc* t, int dt, std::vector<int64_t> shape) {
+    return t != nullptr && t->data != nullptr && t->dtype == dt && t->shape == shape;
+}
+
+int copy2d(void* dst, size_t dpitch, const TensorSrc* src, size_t src_off, size_t spitch, size_t width,
+           size_t height, cudaStream_t s) {
+    const char* p = static_cast<const char*>(src->data) + src_off;
+    const cudaMemcpyKind kind = src->on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    if (height == 0 || width == 0) return 0;
+    if (dpitch == width && spitch == width)
+        return static_cast<int>(cudaMemcpyAsync(dst, p, width * height, kind, s));
+    return static_cast<int>(cudaMemcpy2DAsync(dst, dpitch, p, spitch, width, height, kind, s));
+}
+
+}  // namespace
+
+Qwen3Engine::~Qwen3Engine() {
+    if (graph_fwd_) cudaGraphExecDestroy(graph_fwd_);
+    if (graph_step_) cudaGraphExecDestroy(graph_step_);
+    if (host_state_) cudaFreeHost(host_state_);
+    if (host_token_) cudaFreeHost(host_token_);
+    if (comm_ && nccl().ok) nccl().CommDestroy(comm_);
+}
+
+int Qwen3Engine::create(const Qwen3Dims& d, const std::vector<TensorSrc>& tensors, const EngineOptions& opt,
+                        std::unique_ptr<Qwen3Engine>* out, std::string* err) {
+    auto fail = [&](int code, const std::string& m) {
+        if (err) *err = m;
+        return code;
+    };
+    if (d.vocab <= 0 || d.hidden <= 0 || d.inter <= 0 || d.layers <= 0 || d.q_heads <= 0 || d.kv_heads <= 0 ||
+        d.q_heads % d.kv_heads || d.max_seq <= 0 || !(d.eps > 0.f) || !(d.theta > 0.f))
+        return fail(FIRE_B200_ERR_INVALID, "invalid Qwen3 profile");
+    if (d.head_dim != 128) return fail(FIRE_B200_ERR_UNSUPPORTED, "the decode engine needs head_dim 128");
+    const int t = opt.tp_size;
+    if (t < 1 || opt.tp_rank < 0 || opt.tp_rank >= t) return fail(FIRE_B200_ERR_INVALID, "bad tensor-parallel rank");
+    if (d.q_heads % t || d.kv_heads % t || d.inter % t || d.vocab % t)
+        return fail(FIRE_B200_ERR_UNSUPPORTED, "heads, FFN width and vocab must divide by the TP size");
+    if (d.hidden % 128 || (d.inter / t) % 128 || d.hidden > 53248 || d.inter / t > 53248)
+        return fail(FIRE_B200_ERR_UNSUPPORTED, "hidden and FFN shard must be multiples of the 128 group");
+    if (t > 1 && (opt.nccl_id == nullptr || !nccl().ok))
+        return fail(FIRE_B200_ERR_UNSUPPORTED, "tensor parallel needs NCCL: " + nccl().error);
+
+    std::unique_ptr<Qwen3Engine> e(new Qwen3Engine());
+    e->d_ = d;
+    e->opt_ = opt;
+    e->tp_ = t;
+    e->rank_ = opt.tp_rank;
+    FB_CK(cudaGetDevice(&e->device_));
+    FB_RC(device_sms(&e->sms_));
+    e->hq_ = d.q_heads / t;
+    e->hkv_ = d.kv_heads / t;
+    e->q_ = e->hq_ * 128;
+    e->kv_ = e->hkv_ * 128;
+    e->f_ = d.inter / t;
+    e->v_ = d.vocab / t;
+    e->v_off_ = e->rank_ * e->v_;
+    e->weight_arena_.reset(new DeviceArena(e->device_));
+    e->runtime_arena_.reset(new DeviceArena(e->device_));
+    const int rc = e->import_weights(tensors, err);
+    if (rc != 0) return rc;
+    if (t > 1) {
+        const int nr = nccl_comm_init_rank(&e->comm_, t, opt.nccl_id, e->rank_);
+        if (nr != 0) return fail(FIRE_B200_ERR_STATE, std::string("ncclCommInitRank: ") + nccl().GetErrorString(nr));
+    }
+    *out = std::move(e);
+    return 0;
+}
+
+int Qwen3Engine::import_weights(const std::vector<TensorSrc>& tensors, std::string* err) {
+    auto fail = [&](int code, const std::string& m) {
+        if (err) *err = m;
+        return code;
+    };
+    const Sources S(tensors);
+    const int H = d_.hidden, F = d_.inter, Q = d_.q_heads * 128, KV = d_.kv_heads * 128, V = d_.vocab;
+    const int L = d_.layers;
+
+    // --- validate (Qwen3Loader::load_weights rules, src/model/qwen_loader.cpp:123-223)
+    const TensorSrc* emb = S.get("tok_embeddings.weight");
+    if (!(is(emb, kSrcF32, {V, H}) || is(emb, kSrcBF16, {V, H})))
+        return fail(FIRE_B200_ERR_INVALID, "tok_embeddings.weight must be FP32 or BF16 [vocab, hidden]");
+    auto w4_ok = [&](const std::string& base, int n, int k) {
+        return is(S.get(base + ".qweight"), kSrcU8, {n, k / 2}) && is(S.get(base + ".scales"), kSrcF32, {n, k / 128}) &&
+               is(S.get(base + ".zero_points"), kSrcU8, {n, k / 128});
+    };
+    for (int l = 0; l < L; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        if (!is(S.get(p + "attention_norm.weight"), kSrcF32, {H}) || !is(S.get(p + "ffn_norm.weight"), kSrcF32, {H}) ||
+            !is(S.get(p + "attention.q_norm.weight"), kSrcF32, {128}) ||
+            !is(S.get(p + "attention.k_norm.weight"), kSrcF32, {128}))
+            return fail(FIRE_B200_ERR_INVALID, "bad norm weights in layer " + std::to_string(l));
+        const std::pair<std::string, std::pair<int, int>> mats[] = {
+            {"attention.wq", {Q, H}}, {"attention.wk", {KV, H}}, {"attention.wv", {KV, H}}, {"attention.wo", {H, Q}},
+            {"feed_forward.w1", {F, H}}, {"feed_forward.w2", {H, F}}, {"feed_forward.w3", {F, H}}};
+        for (const auto& m : mats) {
+            if (S.has(p + m.first + ".weight"))
+                return fail(FIRE_B200_ERR_UNSUPPORTED,
+                            "plain FP32 projections are not on the INT4 decode path: " + p + m.first);
+            if (!w4_ok(p + m.first, m.second.first, m.second.second))
+                return fail(FIRE_B200_ERR_INVALID, "bad INT4 group-128 triplet: " + p + m.first);
+        }
+    }
+    if (!is(S.get("norm.weight"), kSrcF32, {H})) return fail(FIRE_B200_ERR_INVALID, "bad norm.weight");
+    const TensorSrc* head = S.get("output.weight");
+    if (head != nullptr) {
+        if (!(is(head, kSrcF32, {V, H}) || is(head, kSrcBF16, {V, H})))
+            return fail(FIRE_B200_ERR_INVALID, "output.weight must be FP32 or BF16 [vocab, hidden]");
+        head_kind_ = head->dtype == kSrcBF16 ? 1 : 0;
+    } else if (w4_ok("output", V, H)) {
+        head_kind_ = 2;
+    } else {
+        return fail(FIRE_B200_ERR_INVALID, "missing LM head (output.weight or output.qweight triplet)");
+    }
+
+    // --- sizes and one reservation
+    auto w4_bytes = [](int n, int k) {
+        return pad256(size_t(n) * k / 2) + pad256(size_t(n) * (k / 128) * 4) + pad256(size_t(n) * (k / 128));
+    };
+    size_t total = pad256(size_t(V) * H * esize(emb->dtype)) + pad256(size_t(H) * 4);
+    const size_t per_layer = w4_bytes(q_ + 2 * kv_, H) + w4_bytes(H, q_) + w4_bytes(2 * f_, H) + w4_bytes(H, f_) +
+                             2 * pad256(size_t(H) * 4) + 2 * pad256(512);
+    total += per_layer * L;
+    total += head_kind_ == 2 ? w4_bytes(v_, H) : pad256(size_t(v_) * H * (head_kind_ == 1 ? 2 : 4));
+    FB_RC(weight_arena_->reserve(total + 4096));
+    weight_bytes_ = total;
+
+    cudaStream_t s;
+    FB_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    auto alloc = [&](size_t b) { return weight_arena_->alloc(b); };
+    int rc = 0;
+    auto whole = [&](const TensorSrc* src, size_t bytes) -> void* {
+        void* p = alloc(bytes);
+        if (!p) { rc = FIRE_B200_ERR_NOMEM; return nullptr; }
+        if (!rc) rc = copy2d(p, bytes, src, 0, bytes, bytes, 1, s);
+        return p;
+    };
+    auto w4_alloc = [&](W4Mat& m, int n, int k) {
+        m.n = n;
+        m.k = k;
+        m.qw = static_cast<uint8_t*>(alloc(size_t(n) * k / 2));
+        m.s = static_cast<float*>(alloc(size_t(n) * (k / 128) * 4));
+        m.z = static_cast<uint8_t*>(alloc(size_t(n) * (k / 128)));
+        if (!m.qw || !m.s || !m.z) rc = FIRE_B200_ERR_NOMEM;
+    };
+    // Copy rows of a global [N, K] INT4 matrix (qweight/scales/zero_points), columns
+    // [c0, c0+kk) of K (group aligned), into `m`: source rows r0 + b*block + r go to
+    // destination rows dst_row + b*dst_stride + r, for r < block and b < rows/block.
+    // block == dst_stride == 1 is a plain row copy; block 2 / stride 4 interleaves
+    // gate and up rows per GEMV tile.
+    auto w4_copy = [&](W4Mat& m, const std::string& base, int K, int r0, int rows, int c0, int kk, int dst_row,
+                       int block, int dst_stride) {
+        const TensorSrc* q = S.get(base + ".qweight");
+        const TensorSrc* sc = S.get(base + ".scales");
+        const TensorSrc* z = S.get(base + ".zero_points");
+        const size_t qrow = size_t(K) / 2, grow = size_t(K) / 128;
+        const size_t dq = size_t(m.k) / 2, dg = size_t(m.k) / 128;
+        const size_t wq = size_t(kk) / 2, wg = size_t(kk) / 128;
+        const int nblocks = rows / block;
+        for (int r = 0; r < block && !rc; ++r) {
+            const size_t sr = size_t(r0) + r, dr = size_t(dst_row) + r;
+            rc = copy2d(m.qw + dr * dq, dq * dst_stride, q, sr * qrow + c0 / 2, qrow * block, wq, nblocks, s);
+            if (!rc)
+                rc = copy2d(reinterpret_cast<char*>(m.s) + dr * dg * 4, dg * 4 * dst_stride, sc,
+                            (sr * grow + c0 / 128) * 4, grow * 4 * block, wg * 4, nblocks, s);
+            if (!rc)
+                rc = copy2d(m.z + dr * dg, dg * dst_stride, z, sr * grow + c0 / 128, grow * block, wg, nblocks, s);
+        }
+    };
+
+    emb_bf16_ = emb->dtype == kSrcBF16;
+    embedding_ = whole(emb, size_t(V) * H * esize(emb->dtype));
+    final_norm_ = static_cast<float*>(whole(S.get("norm.weight"), size_t(H) * 4));
+    layers_.resize(L);
+    const int half = kW4TileRows / 2;
+    for (int l = 0; l < L && !rc; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        Layer& y = layers_[l];
+        y.attn_norm = static_cast<float*>(whole(S.get(p + "attention_norm.weight"), size_t(H) * 4));
+        y.ffn_norm = static_cast<float*>(whole(S.get(p + "ffn_norm.weight"), size_t(H) * 4));
+        y.q_norm = static_cast<float*>(whole(S.get(p + "attention.q_norm.weight"), 512));
+        y.k_norm = static_cast<float*>(whole(S.get(p + "attention.k_norm.weight"), 512));
+        // q/k/v: this rank's heads, concatenated
+        w4_alloc(y.qkv, q_ + 2 * kv_, H);
+        if (!rc) w4_copy(y.qkv, p + "attention.wq", H, rank_ * q_, q_, 0, H, 0, 1, 1);
+        if (!rc) w4_copy(y.qkv, p + "attention.wk", H, rank_ * kv_, kv_, 0, H, q_, 1, 1);
+        if (!rc) w4_copy(y.qkv, p + "attention.wv", H, rank_ * kv_, kv_, 0, H, q_ + kv_, 1, 1);
+        // o: all rows, this rank's K slice (row parallel)
+        w4_alloc(y.o, H, q_);
+        if (!rc) w4_copy(y.o, p + "attention.wo", Q, 0, H, rank_ * q_, q_, 0, 1, 1);
+        // gate/up: this rank's FFN rows, interleaved per GEMV tile (half gate, half up)
+        w4_alloc(y.gu, 2 * f_, H);
+        if (!rc) w4_copy(y.gu, p + "feed_forward.w1", H, rank_ * f_, f_, 0, H, 0, half, kW4TileRows);
+        if (!rc) w4_copy(y.gu, p + "feed_forward.w3", H, rank_ * f_, f_, 0, H, half, half, kW4TileRows);
+        // down: all rows, this rank's K slice
+        w4_alloc(y.down, H, f_);
+        if (!rc) w4_copy(y.down, p + "feed_forward.w2", F, 0, H, rank_ * f_, f_, 0, 1, 1);
+    }
+    if (!rc) {
+        if (head_kind_ == 2) {
+            w4_alloc(head_w4_, v_, H);
+            if (!rc) w4_copy(head_w4_, "output", H, v_off_, v_, 0, H, 0, 1, 1);
+        } else {
+            const size_t rb = size_t(H) * (head_kind_ == 1 ? 2 : 4);
+            head_dense_ = alloc(size_t(v_) * rb);
+            if (!head_dense_) rc = FIRE_B200_ERR_NOMEM;
+            if (!rc) rc = copy2d(head_dense_, rb, head, size_t(v_off_) * rb, rb, rb, v_, s);
+        }
+    }
+    const cudaError_t se = cudaStreamSynchronize(s);
+    cudaStreamDestroy(s);
+    if (rc) return fail(rc, rc == FIRE_B200_ERR_NOMEM ? "device weight reservation exhausted" : "weight upload failed");
+    if (se != cudaSuccess) return static_cast<int>(se);
+
+    // bytes one decode step reads (weights, norms, one embedding row)
+    auto w4b = [](const W4Mat& m) { return size_t(m.n) * m.k / 2 + size_t(m.n) * (m.k / 128) * 5; };
+    size_t b = size_t(H) * esize(emb->dtype) + size_t(H) * 4;
+    for (const auto& y : layers_) b += w4b(y.qkv) + w4b(y.o) + w4b(y.gu) + w4b(y.down) + size_t(2 * H + 256) * 4;
+    b += head_kind_ == 2 ? w4b(head_w4_) : size_t(v_) * H * (head_kind_ == 1 ? 2 : 4);
+    step_weight_bytes_ = b;
+    return 0;
+}
+
+int Qwen3Engine::prepare(int capacity) {
+    if (capacity <= 0 || capacity > d_.max_seq) return FIRE_B200_ERR_INVALID;
+    if (graph_fwd_) { cudaGraphExecDestroy(graph_fwd_); graph_fwd_ = nullptr; }
+    if (graph_step_) { cudaGraphExecDestroy(graph_step_); graph_step_ = nullptr; }
+    runtime_arena_.reset(new DeviceArena(device_));
+    capacity_ = capacity;
+    length_ = 0;
+    max_chunks_ = (capacity + kAttnChunk - 1) / kAttnChunk;
+    const int H = d_.hidden;
+    const size_t kv_elems = size_t(d_.layers) * capacity * kv_;
+    const size_t attn_ws = attention_workspace_bytes(hq_, hkv_, 128, capacity);
+    const size_t am_ws = argmax_workspace_bytes(kMaxSms);
+    size_t total = 0;
+    const size_t sizes[] = {256, size_t(H) * 4 * 5, size_t(q_ + 2 * kv_) * 4, size_t(q_) * 8, size_t(f_) * 4,
+                            size_t(v_) * 4, size_t(d_.vocab) * 4, kv_elems * 8, size_t(capacity) * 64 * 8,
+                            attn_ws, am_ws, 256, 256 * size_t(tp_), size_t(capacity) * 4};
+    for (size_t sz : sizes) total += pad256(sz) + 256;
+    FB_RC(runtime_arena_->reserve(total));
+    auto A = [&](size_t b) { return runtime_arena_->alloc(b); };
+    state_ = static_cast<DecodeState*>(A(sizeof(DecodeState)));
+    hidden_ = static_cast<float*>(A(size_t(H) * 4));
+    attn_res_ = static_cast<float*>(A(size_t(H) * 4));
+    o_part_ = static_cast<float*>(A(size_t(H) * 4));
+    down_part_ = static_cast<float*>(A(size_t(H) * 4));
+    qkv_ = static_cast<float*>(A(size_t(q_ + 2 * kv_) * 4));
+    q_rot_ = static_cast<float*>(A(size_t(q_) * 4));
+    attn_out_ = static_cast<float*>(A(size_t(q_) * 4));
+    act_ = static_cast<float*>(A(size_t(f_) * 4));
+    logits_ = static_cast<float*>(A(size_t(v_) * 4));
+    logits_full_ = tp_ > 1 ? static_cast<float*>(A(size_t(d_.vocab) * 4)) : logits_;
+    kcache_ = static_cast<float*>(A(kv_elems * 4));
+    vcache_ = static_cast<float*>(A(kv_elems * 4));
+    rope_sin_ = static_cast<float*>(A(size_t(capacity) * 64 * 4));
+    rope_cos_ = static_cast<float*>(A(size_t(capacity) * 64 * 4));
+    attn_ws_ = A(attn_ws);
+    argmax_ws_ = A(am_ws);
+    best_local_ = A(kArgmaxPairBytes);
+    best_all_ = A(kArgmaxPairBytes * tp_);
+    tokens_buf_ = static_cast<int32_t*>(A(size_t(capacity) * 4));
+    if (!state_ || !hidden_ || !attn_res_ || !o_part_ || !down_part_ || !qkv_ || !q_rot_ || !attn_out_ || !act_ ||
+        !logits_ || !logits_full_ || !kcache_ || !vcache_ || !rope_sin_ || !rope_cos_ || !attn_ws_ || !argmax_ws_ ||
+        !best_local_ || !best_all_ || !tokens_buf_)
+        return FIRE_B200_ERR_NOMEM;
+    if (!host_state_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_state_), sizeof(DecodeState)));
+    if (!host_token_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_token_), sizeof(int32_t)));
+
+    cudaStream_t s;
+    FB_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    FB_CK(cudaMemsetAsync(state_, 0, sizeof(DecodeState), s));
+    FB_CK(cudaMemsetAsync(attn_ws_, 0, attn_ws, s));
+    FB_CK(cudaMemsetAsync(argmax_ws_, 0, am_ws, s));
+    FB_CK(cudaMemsetAsync(kcache_, 0, kv_elems * 4, s));
+    FB_CK(cudaMemsetAsync(vcache_, 0, kv_elems * 4, s));
+    // RoPE caches for positions 0..capacity-1 (Qwen3Model::prepare, src/model/qwen.cpp:143-149)
+    FB_CK(rope_cache_launch(128, capacity, d_.theta, rope_sin_, rope_cos_, sms_, s));
+    // one eager step: sets kernel attributes and checks every launch before capture
+    int rc = enqueue_step(s, true);
+    if (rc == 0) rc = static_cast<int>(cudaStreamSynchronize(s));
+    if (rc == 0) rc = static_cast<int>(cudaMemsetAsync(state_, 0, sizeof(DecodeState), s));
+    if (rc == 0) rc = static_cast<int>(cudaStreamSynchronize(s));
+    cudaStreamDestroy(s);
+    if (rc) return rc;
+    if (opt_.use_graph) {
+        FB_RC(capture(false, &graph_fwd_));
+        FB_RC(capture(true, &graph_step_));
+    }
+    return 0;
+}
+
+int Qwen3Engine::capture(bool sample, cudaGraphExec_t* exec) {
+    cudaStream_t cs;
+    FB_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+    int rc = e == cudaSuccess ? 0 : static_cast<int>(e);
+    if (!rc) {
+        rc = enqueue_step(cs, sample);
+        e = cudaStreamEndCapture(cs, &g);
+        if (!rc && e != cudaSuccess) rc = static_cast<int>(e);
+    }
+    if (!rc) {
+        e = cudaGraphInstantiate(exec, g, 0);
+        if (e != cudaSuccess) rc = static_cast<int>(e);
+    }
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(cs);
+    return rc;
+}
+
+int Qwen3Engine::enqueue_step(cudaStream_t s, bool sample) {
+    const bool pdl = opt_.pdl;
+    const int H = d_.hidden;
+    auto allreduce = [&](float* buf) -> int {
+        const int r = nccl().AllReduce(buf, buf, size_t(H), kNcclFloat32, 0, comm_, s);
+        return r == 0 ? 0 : FIRE_B200_ERR_STATE;
+    };
+    auto mat = [](W4Args& a, const W4Mat& m) {
+        a.qw = m.qw;
+        a.scales = m.s;
+        a.zeros = m.z;
+        a.N = m.n;
+        a.K = m.k;
+    };
+    FB_CK(embedding_launch(nullptr, 1, state_, embedding_, emb_bf16_, d_.vocab, H, hidden_, s, pdl));
+    for (int l = 0; l < d_.layers; ++l) {
+        const Layer& L = layers_[l];
+        const size_t kv_layer = size_t(l) * capacity_ * kv_;
+        // q/k/v = W_qkv . rmsnorm(h)   (qwen.cpp:196-217)
+        W4Args a{};
+        if (tp_ > 1 && l > 0) {
+            a.x = attn_res_;
+            a.x_add = down_part_;
+            a.x_sum_out = hidden_;
+        } else {
+            a.x = hidden_;
+        }
+        a.norm_w = L.attn_norm;
+        a.eps = d_.eps;
+        mat(a, L.qkv);
+        a.y = qkv_;
+        a.prefetch = 1;
+        FB_CK(w4g128_gemv_launch(a, kW4Store, sms_, s, pdl));
+        // q_norm / k_norm, RoPE, KV write (qwen.cpp:222-240)
+        QkRopeArgs r{};
+        r.qkv = qkv_;
+        r.q_norm = L.q_norm;
+        r.k_norm = L.k_norm;
+        r.rope_sin = rope_sin_;
+        r.rope_cos = rope_cos_;
+        r.q_out = q_rot_;
+        r.key_cache = kcache_ + kv_layer;
+        r.value_cache = vcache_ + kv_layer;
+        r.state = state_;
+        r.q_heads = hq_;
+        r.kv_heads = hkv_;
+        r.capacity = capacity_;
+        r.eps = d_.eps;
+        FB_CK(qk_norm_rope_kv_launch(r, s, pdl));
+        // attention (qwen.cpp:242-247)
+        AttnArgs at{};
+        at.q = q_rot_;
+        at.key_cache = kcache_ + kv_layer;
+        at.value_cache = vcache_ + kv_layer;
+        at.out = attn_out_;
+        at.tickets = static_cast<unsigned*>(attn_ws_);
+        at.part_ml = reinterpret_cast<float*>(static_cast<char*>(attn_ws_) + 256);
+        at.part = at.part_ml + size_t(hq_) * max_chunks_ * 2;
+        at.state = state_;
+        at.q_heads = hq_;
+        at.kv_heads = hkv_;
+        at.hd = 128;
+        at.capacity = capacity_;
+        at.max_chunks = max_chunks_;
+        at.scale = 1.0f / sqrtf(128.0f);
+        FB_CK(attention_launch(at, s, pdl));
+        // o projection + residual (qwen.cpp:249-262)
+        W4Args o{};
+        o.x = attn_out_;
+        mat(o, L.o);
+        o.prefetch = 1;
+        if (tp_ == 1) {
+            o.y = attn_res_;
+            o.residual = hidden_;
+            FB_CK(w4g128_gemv_launch(o, kW4Residual, sms_, s, pdl));
+        } else {
+            o.y = o_part_;
+            FB_CK(w4g128_gemv_launch(o, kW4Store, sms_, s, pdl));
+            FB_RC(allreduce(o_part_));
+        }
+        // gate/up . rmsnorm(attn_res), SwiGLU (qwen.cpp:264-281)
+        W4Args g{};
+        if (tp_ == 1) {
+            g.x = attn_res_;
+        } else {
+            g.x = hidden_;
+            g.x_add = o_part_;
+            g.x_sum_out = attn_res_;
+        }
+        g.norm_w = L.ffn_norm;
+        g.eps = d_.eps;
+        mat(g, L.gu);
+        g.y = act_;
+        g.prefetch = 1;
+        FB_CK(w4g128_gemv_launch(g, kW4Swiglu, sms_, s, pdl));
+        // down + residual (qwen.cpp:282-291)
+        W4Args dn{};
+        dn.x = act_;
+        mat(dn, L.down);
+        dn.prefetch = 1;
+        if (tp_ == 1) {
+            dn.y = hidden_;
+            dn.residual = attn_res_;
+            FB_CK(w4g128_gemv_launch(dn, kW4Residual, sms_, s, pdl));
+        } else {
+            dn.y = down_part_;
+            FB_CK(w4g128_gemv_launch(dn, kW4Store, sms_, s, pdl));
+            FB_RC(allreduce(down_part_));
+        }
+    }
+    // final norm + LM head (qwen.cpp:294-301)
+    const float* hx = tp_ > 1 ? attn_res_ : hidden_;
+    const float* hadd = tp_ > 1 ? down_part_ : nullptr;
+    float* hsum = tp_ > 1 ? hidden_ : nullptr;
+    if (head_kind_ == 2) {
+        W4Args h{};
+        h.x = hx;
+        h.x_add = hadd;
+        h.x_sum_out = hsum;
+        h.norm_w = final_norm_;
+        h.eps = d_.eps;
+        mat(h, head_w4_);
+        h.y = logits_;
+        h.prefetch = 1;
+        FB_CK(w4g128_gemv_launch(h, kW4Store, sms_, s, pdl));
+    } else {
+        DenseArgs h{};
+        h.x = hx;
+        h.x_add = hadd;
+        h.x_sum_out = hsum;
+        h.norm_w = final_norm_;
+        h.eps = d_.eps;
+        h.w = head_dense_;
+        h.scale = 1.0f;
+        h.y = logits_;
+        h.N = v_;
+        h.K = H;
+        h.prefetch = 1;
+        FB_CK(dense_gemv_launch(h, head_kind_ == 1, sms_, s, pdl));
+    }
+    const int am_sms = sms_ < kMaxSms ? sms_ : kMaxSms;
+    if (sample) {
+        if (tp_ == 1) {
+            FB_CK(argmax_launch(logits_, v_, argmax_ws_, am_sms, nullptr, state_, tokens_buf_, capacity_, s, pdl));
+        } else {
+            FB_CK(argmax_launch(logits_, v_, argmax_ws_, am_sms, nullptr, nullptr, nullptr, 0, s, pdl, v_off_,
+                                best_local_));
+            const int r = nccl().AllGather(best_local_, best_all_, kArgmaxPairBytes, kNcclUint8, comm_, s);
+            if (r != 0) return FIRE_B200_ERR_STATE;
+            FB_CK(argmax_select_launch(best_all_, tp_, state_, tokens_buf_, capacity_, s, pdl));
+        }
+    } else if (tp_ > 1) {
+        const int r = nccl().AllGather(logits_, logits_full_, size_t(v_), kNcclFloat32, comm_, s);
+        if (r != 0) return FIRE_B200_ERR_STATE;
+    }
+    return 0;
+}
+
+int Qwen3Engine::launch_step(cudaStream_t s, bool sample) {
+    cudaGraphExec_t g = sample ? graph_step_ : graph_fwd_;
+    if (g) return static_cast<int>(cudaGraphLaunch(g, s));
+    return enqueue_step(s, sample);
+}
+
+int Qwen3Engine::kernels_per_step() const { return 6 * d_.layers + 3 + (tp_ > 1 ? 1 : 0); }
+
+int Qwen3Engine::forward(int token, int pos, float* logits_out, cudaStream_t s) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (token < 0 || token >= d_.vocab) return FIRE_B200_ERR_INVALID;
+    if (pos != length_ || pos < 0 || pos >= capacity_) return FIRE_B200_ERR_STATE;
+    FB_CK(set_state_launch(state_, token, pos, 0, s, false));
+    FB_RC(launch_step(s, false));
+    if (logits_out != nullptr && logits_out != logits())
+        FB_CK(cudaMemcpyAsync(logits_out, logits(), size_t(d_.vocab) * 4, cudaMemcpyDeviceToDevice, s));
+    ++length_;  // KVCache::commit (src/model/kv_cache.cpp:76-83)
+    return 0;
+}
+
+int Qwen3Engine::generate(int first_token, int steps, int32_t* tokens_out, cudaStream_t s) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (first_token < 0 || first_token >= d_.vocab || steps < 1) return FIRE_B200_ERR_INVALID;
+    if (length_ + steps > capacity_) return FIRE_B200_ERR_STATE;
+    FB_CK(set_state_launch(state_, first_token, length_, 0, s, false));
+    for (int i = 0; i < steps; ++i) FB_RC(launch_step(s, true));
+    if (tokens_out != nullptr && tokens_out != tokens_buf_)
+        FB_CK(cudaMemcpyAsync(tokens_out, tokens_buf_, size_t(steps) * 4, cudaMemcpyDeviceToDevice, s));
+    length_ += steps;
+    return 0;
+}
+
+int Qwen3Engine::generate_host(const int32_t* prompt, int n_prompt, int steps, int32_t* out_host, cudaStream_t s) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (!prompt || n_prompt < 1 || steps < 1 || !out_host) return FIRE_B200_ERR_INVALID;
+    if (length_ + n_prompt + steps - 1 > capacity_) return FIRE_B200_ERR_STATE;
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d_.vocab) return FIRE_B200_ERR_INVALID;
+    for (int i = 0; i + 1 < n_prompt; ++i) {
+        FB_CK(set_state_launch(state_, prompt[i], length_, 0, s, false));
+        FB_RC(launch_step(s, false));
+        ++length_;
+    }
+    int32_t token = prompt[n_prompt - 1];
+    for (int i = 0; i < steps; ++i) {
+        // H2D of this step's input from pinned memory, one step, D2H of the sample.
+        *host_state_ = DecodeState{token, length_, 0, 0};
+        FB_CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, s));
+        FB_RC(launch_step(s, true));
+        FB_CK(cudaMemcpyAsync(host_token_, &state_->token, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+        FB_CK(cudaStreamSynchronize(s));
+        token = *host_token_;
+        out_host[i] = token;
+        ++length_;  // the step consumed its input (n_prompt + steps - 1 tokens in all)
+    }
+    return 0;
+}
+
+int Qwen3Engine::truncate(int length) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (length < 0 || length > length_) return FIRE_B200_ERR_INVALID;
+    length_ = length;
+    return 0;
+}
+
+int Qwen3Engine::reset() {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    length_ = 0;  // KVCache::reset (src/model/kv_cache.cpp:85)
+    return 0;
+}
+
+}  // namespace fb

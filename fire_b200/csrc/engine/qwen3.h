@@ -1,0 +1,148 @@
+// Qwen3 single-token decode engine (the B200 implementation behind Fire's
+// Qwen3Model, src/model/qwen.cpp:30-303, and Qwen3Loader, src/model/qwen_loader.cpp).
+//
+// One engine serves one sequence on one GPU, or one tensor-parallel rank of it.
+// Weights are imported once into a device arena and repacked for the kernels:
+//   * q/k/v rows concatenated into one INT4 matrix (one GEMV launch per layer);
+//   * gate/up rows interleaved per GEMV tile (the SwiGLU epilogue sees both halves);
+//   * tensor parallel: column-parallel q/k/v/gate/up (heads / FFN rows), row-parallel
+//     o/down (group-aligned K slices), vocab-sharded LM head, replicated embedding and
+//     norms, KV cache sharded by KV head.
+// A decode step is a fixed launch sequence that reads the token and position from a
+// device-resident control block, so it is captured once in a CUDA graph and replayed:
+//   embedding -> per layer [qkv GEMV (RMSNorm prologue) -> q/k-norm+RoPE+KV write ->
+//   split-K attention -> o GEMV (+residual) -> gate/up GEMV (RMSNorm prologue, SwiGLU
+//   epilogue) -> down GEMV (+residual)] -> LM head (final-norm prologue) -> argmax.
+// Under tensor parallelism the o/down partial sums go through an NCCL all-reduce and
+// the residual add moves into the next GEMV's prologue; sampling all-gathers one
+// (max, index) pair per rank.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "engine/arena.h"
+#include "engine/nccl_shim.h"
+#include "kernels/decode_state.h"
+
+namespace fb {
+
+struct Qwen3Dims {
+    int vocab = 0, max_seq = 0, hidden = 0, inter = 0, layers = 0, q_heads = 0, kv_heads = 0, head_dim = 0;
+    float eps = 0.f, theta = 0.f;
+};
+
+enum SrcDType : int { kSrcF32 = 0, kSrcBF16 = 1, kSrcU8 = 2 };
+
+// One tensor of a Fire checkpoint (names as in tools/export_qwen3.py), host or device.
+struct TensorSrc {
+    std::string name;
+    int dtype = kSrcF32;
+    std::vector<int64_t> shape;
+    const void* data = nullptr;
+    bool on_device = false;
+};
+
+struct EngineOptions {
+    int tp_rank = 0, tp_size = 1;
+    const void* nccl_id = nullptr;  // 128-byte ncclUniqueId shared by all ranks (tp_size > 1)
+    bool use_graph = true;
+    bool pdl = true;
+};
+
+struct W4Mat {
+    uint8_t* qw = nullptr;
+    float* s = nullptr;
+    uint8_t* z = nullptr;
+    int n = 0, k = 0;
+};
+
+class Qwen3Engine {
+  public:
+    static int create(const Qwen3Dims& dims, const std::vector<TensorSrc>& tensors, const EngineOptions& opt,
+                      std::unique_ptr<Qwen3Engine>* out, std::string* err);
+    ~Qwen3Engine();
+
+    // Model::prepare (include/Fire/model/model.h:25-29): runtime buffers, KV cache,
+    // RoPE caches and the captured step graphs for 1 <= capacity <= max_seq.
+    int prepare(int capacity);
+    // Model::forward: consume `token` at `pos` (== length), logits [vocab] into the
+    // engine buffer and, if given, into `logits_out` (device). Asynchronous on `s`.
+    int forward(int token, int pos, float* logits_out, cudaStream_t s);
+    // Greedy decode on the device: `steps` tokens starting from `first_token` at the
+    // current length; tokens_out (device int32 [steps]) receives the sampled ids.
+    // No host synchronisation between tokens.
+    int generate(int first_token, int steps, int32_t* tokens_out, cudaStream_t s);
+    // The reference's host loop (demo/qwen_chat.cpp:231-294): per token an H2D copy of
+    // the token id from pinned memory, one step, a D2H copy of the sampled id and a
+    // stream synchronisation. Prompt tokens are consumed first (no sampling until the
+    // last one); out_host receives `steps` sampled ids.
+    int generate_host(const int32_t* prompt, int n_prompt, int steps, int32_t* out_host, cudaStream_t s);
+    int reset();
+    int truncate(int length);
+
+    int length() const { return length_; }
+    int capacity() const { return capacity_; }
+    const float* logits() const { return tp_ > 1 ? logits_full_ : logits_; }
+    size_t weight_bytes() const { return weight_bytes_; }
+    size_t runtime_bytes() const { return runtime_arena_ ? runtime_arena_->used() : 0; }
+    // Kernels of this library launched per decode step with sampling (graph nodes).
+    int kernels_per_step() const;
+    // Bytes of weights one decode step reads on this rank (the roofline numerator).
+    size_t step_weight_bytes() const { return step_weight_bytes_; }
+    int tp_size() const { return tp_; }
+    int tp_rank() const { return rank_; }
+
+  private:
+    Qwen3Engine() = default;
+    int import_weights(const std::vector<TensorSrc>& tensors, std::string* err);
+    int enqueue_step(cudaStream_t s, bool sample);
+    int capture(bool sample, cudaGraphExec_t* exec);
+    int launch_step(cudaStream_t s, bool sample);
+
+    Qwen3Dims d_;
+    EngineOptions opt_;
+    int device_ = 0, sms_ = 0;
+    int tp_ = 1, rank_ = 0;
+    // per-rank dimensions
+    int hq_ = 0, hkv_ = 0, q_ = 0, kv_ = 0, f_ = 0, v_ = 0, v_off_ = 0;
+
+    std::unique_ptr<DeviceArena> weight_arena_, runtime_arena_;
+    size_t weight_bytes_ = 0, step_weight_bytes_ = 0;
+
+    struct Layer {
+        float* attn_norm = nullptr;
+        float* q_norm = nullptr;
+        float* k_norm = nullptr;
+        float* ffn_norm = nullptr;
+        W4Mat qkv, o, gu, down;
+    };
+    std::vector<Layer> layers_;
+    void* embedding_ = nullptr;
+    bool emb_bf16_ = false;
+    float* final_norm_ = nullptr;
+    int head_kind_ = 0;  // 0 FP32 dense, 1 BF16 dense, 2 INT4
+    W4Mat head_w4_;
+    void* head_dense_ = nullptr;
+
+    // runtime
+    int capacity_ = 0, length_ = 0, max_chunks_ = 0;
+    DecodeState* state_ = nullptr;
+    float *hidden_ = nullptr, *attn_res_ = nullptr, *qkv_ = nullptr, *q_rot_ = nullptr, *attn_out_ = nullptr;
+    float *o_part_ = nullptr, *act_ = nullptr, *down_part_ = nullptr, *logits_ = nullptr, *logits_full_ = nullptr;
+    float *kcache_ = nullptr, *vcache_ = nullptr, *rope_sin_ = nullptr, *rope_cos_ = nullptr;
+    void* attn_ws_ = nullptr;
+    void* argmax_ws_ = nullptr;
+    void* best_local_ = nullptr;
+    void* best_all_ = nullptr;
+    int32_t* tokens_buf_ = nullptr;
+    DecodeState* host_state_ = nullptr;  // pinned, for generate_host
+    int32_t* host_token_ = nullptr;      // pinned
+    cudaGraphExec_t graph_fwd_ = nullptr, graph_step_ = nullptr;
+    NcclComm comm_ = nullptr;
+};
+
+}  // namespace fb

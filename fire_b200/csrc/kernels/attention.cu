@@ -159,9 +159,9 @@ cudaError_t attention_launch(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const size_t smem = (static_cast<size_t>(G) * a.hd + static_cast<size_t>(kAttnChunk) * (a.hd + 1) +
                          static_cast<size_t>(G) * kAttnChunk + 2 * G + static_cast<size_t>(G) * a.max_chunks) *
                         sizeof(float);
-    if (smem > 48 * 1024) {
+    if (smem > 46 * 1024) {  // static shared memory also counts against the 48 KiB default
         cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             227 * 1024);
+                                                 static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};

@@ -60,4 +60,14 @@ __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
 
+// Element i of the GEMV input: x[i] (+ x_add[i]); CTA 0 also records the sum.
+__device__ __forceinline__ float load_input(const float* x, const float* x_add, float* x_sum_out, int i) {
+    float v = x[i];
+    if (x_add != nullptr) {
+        v = __fadd_rn(v, x_add[i]);
+        if (x_sum_out != nullptr && blockIdx.x == 0) x_sum_out[i] = v;
+    }
+    return v;
+}
+
 }  // namespace fb

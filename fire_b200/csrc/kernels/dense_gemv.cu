@@ -42,12 +42,18 @@ __global__ void __launch_bounds__(kThreads, 1) dense_gemv_kernel(const DenseArgs
     if (a.norm_w != nullptr) {
         __shared__ float red[32];
         float ss = 0.0f;
-        for (int k = threadIdx.x; k < K; k += blockDim.x) ss = fmaf(a.x[k], a.x[k], ss);
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            const float v = a.x_add != nullptr ? __fadd_rn(a.x[k], a.x_add[k]) : a.x[k];
+            ss = fmaf(v, v, ss);
+        }
         ss = block_sum(ss, red);
         nscale = 1.0f / sqrtf(ss / static_cast<float>(K) + a.eps);
     }
     for (int k4 = threadIdx.x; k4 < (K >> 2); k4 += blockDim.x) {
-        float4 v = make_float4(a.x[4 * k4], a.x[4 * k4 + 1], a.x[4 * k4 + 2], a.x[4 * k4 + 3]);
+        float4 v = make_float4(load_input(a.x, a.x_add, a.x_sum_out, 4 * k4),
+                               load_input(a.x, a.x_add, a.x_sum_out, 4 * k4 + 1),
+                               load_input(a.x, a.x_add, a.x_sum_out, 4 * k4 + 2),
+                               load_input(a.x, a.x_add, a.x_sum_out, 4 * k4 + 3));
         if (a.norm_w != nullptr) {
             const float* nw = a.norm_w + 4 * k4;
             v = make_float4(v.x * nw[0] * nscale, v.y * nw[1] * nscale, v.z * nw[2] * nscale,
@@ -145,8 +151,9 @@ template <int R, bool BF16>
 cudaError_t launch_t(const DenseArgs& a, int num_sms, cudaStream_t stream, bool pdl) {
     auto kern = dense_gemv_kernel<R, BF16>;
     const int smem = a.K * 4;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (smem > 46 * 1024) {  // static shared memory also counts against the 48 KiB default
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
     const int tiles = (a.N + R - 1) / R;

@@ -7,6 +7,8 @@ namespace fb {
 
 struct DenseArgs {
     const float* x;   // [K] (the raw hidden state when norm_w is set)
+    const float* x_add;   // optional [K]: the input is x + x_add
+    float* x_sum_out;     // optional [K]: CTA 0 stores x + x_add here
     const float* norm_w;  // optional RMSNorm weight [K] applied to x first
     float eps;
     const void* w;    // [N, K] BF16 bits or FP32, 16-byte aligned, K % 8 == 0

@@ -194,9 +194,16 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
     if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
 }
 
+__device__ __forceinline__ void advance_state(DecodeState* state, int32_t* tokens_out, int max_steps, int tok) {
+    if (tokens_out != nullptr && state->step < max_steps) tokens_out[state->step] = tok;
+    state->step += 1;
+    state->token = tok;
+    state->pos += 1;
+}
+
 __global__ void argmax_kernel(const float* __restrict__ x, int n, ArgmaxPart* parts,
                               unsigned* ticket, int64_t* out_index, DecodeState* state,
-                              int32_t* tokens_out, int max_steps) {
+                              int32_t* tokens_out, int max_steps, int base_index, ArgmaxPart* best_out) {
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ bool last;
@@ -232,16 +239,39 @@ __global__ void argmax_kernel(const float* __restrict__ x, int n, ArgmaxPart* pa
             better(fv, fi, v, i);
         }
         if (fi == 0x7fffffff) fi = 0;  // all NaN / -inf: index 0, as a scan from 0 would give
+        fi += base_index;
         if (out_index != nullptr) *out_index = fi;
-        if (state != nullptr) {
-            if (tokens_out != nullptr && state->step < max_steps) tokens_out[state->step] = fi;
-            state->step += 1;
-            state->token = fi;
-            state->pos += 1;
+        if (best_out != nullptr) {
+            *best_out = ArgmaxPart{fv, fi};
+        } else if (state != nullptr) {
+            advance_state(state, tokens_out, max_steps, fi);
         }
         *ticket = 0u;  // leave the workspace ready for the next launch
     }
     pdl_launch_dependents();
+}
+
+// Tensor-parallel sampling: each rank's (max, global index) pair, gathered in rank
+// order, folded with the same first-maximum rule (a lower rank holds lower indices).
+__global__ void argmax_select_kernel(const ArgmaxPart* parts, int count, DecodeState* state,
+                                     int32_t* tokens_out, int max_steps) {
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < count; ++r) better(bv, bi, parts[r].v, parts[r].i);
+    if (bi == 0x7fffffff) bi = 0;
+    advance_state(state, tokens_out, max_steps, bi);
+}
+
+// Sets the decode control block from host values passed as kernel arguments, so a
+// host-driven step needs no host buffer that must outlive the launch.
+__global__ void set_state_kernel(DecodeState* state, int token, int pos, int step) {
+    pdl_wait();
+    state->token = token;
+    state->pos = pos;
+    state->step = step;
+    state->error = 0;
 }
 
 cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
@@ -327,7 +357,7 @@ size_t argmax_workspace_bytes(int num_sms) {
 
 cudaError_t argmax_launch(const float* x, int n, void* workspace, int num_sms, int64_t* out_index,
                           DecodeState* state, int32_t* tokens_out, int max_steps, cudaStream_t s,
-                          bool pdl) {
+                          bool pdl, int base_index, void* best_out) {
     // layout: [ticket (256 B, zero before first use)][parts]
     unsigned* ticket = static_cast<unsigned*>(workspace);
     ArgmaxPart* parts = reinterpret_cast<ArgmaxPart*>(static_cast<char*>(workspace) + 256);
@@ -336,7 +366,21 @@ cudaError_t argmax_launch(const float* x, int n, void* workspace, int num_sms, i
     cudaLaunchAttribute attr[1];
     auto cfg = make_cfg(dim3(blocks), dim3(1024), 0, s, pdl, attr);
     return cudaLaunchKernelEx(&cfg, argmax_kernel, x, n, parts, ticket, out_index, state, tokens_out,
-                              max_steps);
+                              max_steps, base_index, static_cast<ArgmaxPart*>(best_out));
+}
+
+cudaError_t argmax_select_launch(const void* parts, int count, DecodeState* state, int32_t* tokens_out,
+                                 int max_steps, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    auto cfg = make_cfg(dim3(1), dim3(32), 0, s, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, argmax_select_kernel, static_cast<const ArgmaxPart*>(parts), count, state,
+                              tokens_out, max_steps);
+}
+
+cudaError_t set_state_launch(DecodeState* state, int token, int pos, int step, cudaStream_t s, bool pdl) {
+    cudaLaunchAttribute attr[1];
+    auto cfg = make_cfg(dim3(1), dim3(1), 0, s, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, set_state_kernel, state, token, pos, step);
 }
 
 }  // namespace fb

@@ -54,9 +54,17 @@ cudaError_t embedding_launch(const int32_t* tokens, int count, DecodeState* stat
 cudaError_t swiglu_launch(const float* g, const float* u, float* o, int n, int num_sms, cudaStream_t s);
 cudaError_t add_launch(const float* a, const float* b, float* o, int n, int num_sms, cudaStream_t s);
 size_t argmax_workspace_bytes(int num_sms);
+// First index of the maximum of x[0..n). Result: *out_index (if given) and either
+// best_out (an 8-byte {float value; int32 index} pair, index offset by base_index) or,
+// without best_out, the decode state advanced to the sampled token.
 cudaError_t argmax_launch(const float* x, int n, void* workspace, int num_sms, int64_t* out_index,
                           DecodeState* state, int32_t* tokens_out, int max_steps, cudaStream_t s,
-                          bool pdl);
+                          bool pdl, int base_index = 0, void* best_out = nullptr);
+constexpr size_t kArgmaxPairBytes = 8;
+// Folds `count` gathered pairs (rank order) and advances the decode state.
+cudaError_t argmax_select_launch(const void* parts, int count, DecodeState* state, int32_t* tokens_out,
+                                 int max_steps, cudaStream_t s, bool pdl);
+cudaError_t set_state_launch(DecodeState* state, int token, int pos, int step, cudaStream_t s, bool pdl);
 
 size_t attention_workspace_bytes(int q_heads, int kv_heads, int hd, int capacity);
 cudaError_t attention_launch(const AttnArgs& a, cudaStream_t s, bool pdl);

@@ -34,27 +34,29 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr uint32_t kMagic = 0x4B000000u;  // float 2^23
 
-__device__ __forceinline__ float2 magic2(uint32_t a, uint32_t b) {
-    return make_float2(__uint_as_float(a | kMagic), __uint_as_float(b | kMagic));
+// (v & mask) | magic in one LOP3 (LUT 0xEA = (a & b) | c). `magic` arrives in a
+// register (a kernel argument), so the mask is the instruction's only immediate.
+template <uint32_t kMask>
+__device__ __forceinline__ float nib(uint32_t v, uint32_t magic) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "n"(kMask), "r"(magic));
+    return __uint_as_float(r);
 }
 
-// sum over the 32 weights of one 16-byte chunk of x'[k] * (q[k]-z)*16^p(k)
-// where x' = x * 16^-p(k) (pre-scaled in shared memory).
-__device__ __forceinline__ float chunk_dot(const uint4 w, const uint32_t z, const float4* xv) {
-    const float2 n01 = make_float2(-__uint_as_float(kMagic | z), -__uint_as_float(kMagic | (z << 4)));
-    const float2 n23 = make_float2(-__uint_as_float(kMagic | (z << 8)),
-                                   -__uint_as_float(kMagic | (z << 12)));
-    const float2 n42 = make_float2(-__uint_as_float(kMagic | (z << 16)), n23.x);
-    const float2 n34 = make_float2(n23.y, n42.x);
-    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+// sum_k x'[k] * q[k]*16^p(k) over the 32 weights of one 16-byte chunk, added to
+// `init`, where x' = x * 16^-p(k) (pre-scaled in shared memory): each nibble becomes
+// the exact float 2^23 + q*16^p and one packed add of -2^23 leaves q*16^p exactly.
+__device__ __forceinline__ float chunk_dot(const uint4 w, const float4* xv, float init, uint32_t magic) {
+    const float2 nm = make_float2(-8388608.0f, -8388608.0f);
+    float2 acc0 = make_float2(init, 0.f), acc1 = make_float2(0.f, 0.f);
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
         const uint32_t v = ws[m], t = v >> 12;
-        const float2 d01 = __fadd2_rn(magic2(v & 0xFu, v & 0xF0u), n01);
-        const float2 d23 = __fadd2_rn(magic2(v & 0xF00u, v & 0xF000u), n23);
-        const float2 d45 = __fadd2_rn(magic2(v & 0xF0000u, t & 0xF00u), n42);
-        const float2 d67 = __fadd2_rn(magic2(t & 0xF000u, t & 0xF0000u), n34);
+        const float2 d01 = __fadd2_rn(make_float2(nib<0xFu>(v, magic), nib<0xF0u>(v, magic)), nm);
+        const float2 d23 = __fadd2_rn(make_float2(nib<0xF00u>(v, magic), nib<0xF000u>(v, magic)), nm);
+        const float2 d45 = __fadd2_rn(make_float2(nib<0xF0000u>(v, magic), nib<0xF00u>(t, magic)), nm);
+        const float2 d67 = __fadd2_rn(make_float2(nib<0xF000u>(t, magic), nib<0xF0000u>(t, magic)), nm);
         const float4 xa = xv[2 * m], xb = xv[2 * m + 1];
         acc0 = __ffma2_rn(make_float2(xa.x, xa.y), d01, acc0);
         acc1 = __ffma2_rn(make_float2(xa.z, xa.w), d23, acc1);
@@ -64,38 +66,72 @@ __device__ __forceinline__ float chunk_dot(const uint4 w, const uint32_t z, cons
     return (acc0.x + acc1.x) + (acc0.y + acc1.y);
 }
 
-// Stage x (optionally RMS-normalised) into xs[i][c], scaled by 16^-p.
-__device__ __forceinline__ void stage_x(const W4Args& a, float4* xs, float* red) {
+// Stage x (optionally residual-summed and RMS-normalised) into xs[i][c] scaled by
+// 16^-p, and the plain per-chunk sums xsum[c] = sum of the chunk's 32 x values.
+__device__ __forceinline__ void stage_x(const W4Args& a, float4* xs, float* xsum, float* red) {
     const int K = a.K, chunks = K >> 5;
     float scale = 1.0f;
     if (a.norm_w != nullptr) {
         float ss = 0.0f;
         for (int k = threadIdx.x; k < K; k += blockDim.x) {
-            const float v = a.x[k];
+            const float v = a.x_add != nullptr ? __fadd_rn(a.x[k], a.x_add[k]) : a.x[k];
             ss = fmaf(v, v, ss);
         }
         ss = block_sum(ss, red);
         scale = 1.0f / sqrtf(ss / static_cast<float>(K) + a.eps);
     }
-    for (int k4 = threadIdx.x; k4 < (K >> 2); k4 += blockDim.x) {
-        float4 v = make_float4(a.x[4 * k4], a.x[4 * k4 + 1], a.x[4 * k4 + 2], a.x[4 * k4 + 3]);
-        if (a.norm_w != nullptr) {
-            const float* w = a.norm_w + 4 * k4;
-            v = make_float4(v.x * w[0] * scale, v.y * w[1] * scale, v.z * w[2] * scale,
-                            v.w * w[3] * scale);
+    // one warp per chunk at a time: lane l < 8 handles float4 l of the chunk
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int c0 = warp * 4; c0 < chunks; c0 += nwarps * 4) {
+        const int c = c0 + (lane >> 3), i = lane & 7;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < chunks) {
+            const int k = c * 32 + 4 * i;
+            v = make_float4(load_input(a.x, a.x_add, a.x_sum_out, k), load_input(a.x, a.x_add, a.x_sum_out, k + 1),
+                            load_input(a.x, a.x_add, a.x_sum_out, k + 2), load_input(a.x, a.x_add, a.x_sum_out, k + 3));
+            if (a.norm_w != nullptr) {
+                const float* w = a.norm_w + k;
+                v = make_float4(v.x * w[0] * scale, v.y * w[1] * scale, v.z * w[2] * scale, v.w * w[3] * scale);
+            }
         }
-        const int i = k4 & 7, c = k4 >> 3;
-        if ((i & 1) == 0) {
-            v.y *= 0.0625f;
-            v.z *= 0.00390625f;
-            v.w *= 0.000244140625f;
-        } else {
-            v.x *= 1.52587890625e-05f;
-            v.y *= 0.00390625f;
-            v.z *= 0.000244140625f;
-            v.w *= 1.52587890625e-05f;
+        // chunk sum over the 8 lanes of this chunk (fixed order: pairs, then tree)
+        float cs = (v.x + v.y) + (v.z + v.w);
+        cs += __shfl_xor_sync(0xffffffffu, cs, 1);
+        cs += __shfl_xor_sync(0xffffffffu, cs, 2);
+        cs += __shfl_xor_sync(0xffffffffu, cs, 4);
+        if (c < chunks) {
+            if (i == 0) xsum[c] = cs;
+            if ((i & 1) == 0) {
+                v.y *= 0.0625f;
+                v.z *= 0.00390625f;
+                v.w *= 0.000244140625f;
+            } else {
+                v.x *= 1.52587890625e-05f;
+                v.y *= 0.00390625f;
+                v.z *= 0.000244140625f;
+                v.w *= 1.52587890625e-05f;
+            }
+            xs[i * chunks + c] = v;
         }
-        xs[i * chunks + c] = v;
+    }
+}
+
+struct Stage {
+    uint4 w[kW4TileRows];
+    float s[kW4TileRows];
+    uint32_t z[kW4TileRows];
+};
+
+template <int R>
+__device__ __forceinline__ void load_stage(Stage& st, const W4Args& a, int row0, int c, size_t row_bytes,
+                                           int groups) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int row = min(row0 + r, a.N - 1);
+        st.w[r] = ldg_stream(a.qw + static_cast<size_t>(row) * row_bytes + static_cast<size_t>(c) * 16);
+        const size_t mi = static_cast<size_t>(row) * groups + (c >> 2);
+        st.s[r] = __ldg(a.scales + mi);
+        st.z[r] = __ldg(a.zeros + mi);
     }
 }
 
@@ -105,109 +141,103 @@ __global__ void __launch_bounds__(kThreads, 1) w4g128_gemv_kernel(const W4Args a
     __shared__ float red[32];
     const int K = a.K, N = a.N;
     const int chunks = K >> 5, groups = K >> 7;
+    float* xsum = reinterpret_cast<float*>(xs + (K >> 2));
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tiles = (N + R - 1) / R;
     const size_t row_bytes = static_cast<size_t>(K) >> 1;
+    const uint32_t magic = a.magic;
 
-    // Weights never depend on the previous kernel: start pulling this CTA's first
-    // tiles into L2 before waiting for x.
-    if (a.prefetch && lane == 0) {
-        const int t = blockIdx.x + gridDim.x * warp;
-        if (t < tiles) {
-            const int rows = min(R, N - t * R);
-            prefetch_l2_bulk(a.qw + static_cast<size_t>(t) * R * row_bytes,
-                             static_cast<uint32_t>(rows * row_bytes));
-        }
+    // Weights never depend on the previous kernel: start pulling this warp's first
+    // tile into L2 before waiting for x.
+    const int t_first = blockIdx.x + gridDim.x * warp;
+    const int t_stride = gridDim.x * kWarps;
+    if (a.prefetch && lane == 0 && t_first < tiles) {
+        const int rows = min(R, N - t_first * R);
+        prefetch_l2_bulk(a.qw + static_cast<size_t>(t_first) * R * row_bytes, static_cast<uint32_t>(rows * row_bytes));
     }
     pdl_wait();
-    stage_x(a, xs, red);
+    stage_x(a, xs, xsum, red);
     __syncthreads();
     pdl_launch_dependents();
+    if (t_first >= tiles) return;
 
-    for (int t = blockIdx.x + gridDim.x * warp; t < tiles; t += gridDim.x * kWarps) {
-        const int row0 = t * R;
-        float acc[R];
+    // Work items of this warp: (tile, chunk-slot) in order; one item of look-ahead.
+    const int per_tile = (chunks + 31) >> 5;  // chunk slots per lane per tile
+    const int my_tiles = (tiles - t_first + t_stride - 1) / t_stride;
+    const int items = my_tiles * per_tile;
+    Stage cur, nxt;
+    {
+        const int c = lane;
+        if (c < chunks) load_stage<R>(cur, a, t_first * R, c, row_bytes, groups);
+    }
+    float acc[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-
-        for (int c0 = lane; c0 < chunks; c0 += 64) {
-            const int c1 = c0 + 32;
-            const bool has1 = c1 < chunks;
-            uint4 w0[R], w1[R];
-            float s0[R], s1[R];
-            uint32_t z0[R], z1[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int row = min(row0 + r, N - 1);
-                const uint8_t* qrow = a.qw + static_cast<size_t>(row) * row_bytes;
-                const size_t mrow = static_cast<size_t>(row) * groups;
-                w0[r] = ldg_stream(qrow + static_cast<size_t>(c0) * 16);
-                s0[r] = __ldg(a.scales + mrow + (c0 >> 2));
-                z0[r] = __ldg(a.zeros + mrow + (c0 >> 2));
-                if (has1) {
-                    w1[r] = ldg_stream(qrow + static_cast<size_t>(c1) * 16);
-                    s1[r] = __ldg(a.scales + mrow + (c1 >> 2));
-                    z1[r] = __ldg(a.zeros + mrow + (c1 >> 2));
-                }
-            }
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    for (int it = 0; it < items; ++it) {
+        const int tj = it / per_tile, slot = it - tj * per_tile;
+        const int t = t_first + tj * t_stride;
+        const int c = lane + 32 * slot;
+        if (it + 1 < items) {
+            const int tj1 = (it + 1) / per_tile, slot1 = it + 1 - tj1 * per_tile;
+            const int c1 = lane + 32 * slot1;
+            if (c1 < chunks) load_stage<R>(nxt, a, (t_first + tj1 * t_stride) * R, c1, row_bytes, groups);
+        }
+        if (c < chunks) {
             float4 xv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xv[i] = xs[i * chunks + c0];
+            for (int i = 0; i < 8; ++i) xv[i] = xs[i * chunks + c];
+            const float xc = xsum[c];
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[r] = fmaf(s0[r], chunk_dot(w0[r], z0[r], xv), acc[r]);
-            if (has1) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xv[i] = xs[i * chunks + c1];
-#pragma unroll
-                for (int r = 0; r < R; ++r)
-                    acc[r] = fmaf(s1[r], chunk_dot(w1[r], z1[r], xv), acc[r]);
+            for (int r = 0; r < R; ++r) {
+                const float zf = __uint_as_float(cur.z[r] | 0x4B000000u) - 8388608.0f;
+                acc[r] = fmaf(cur.s[r], chunk_dot(cur.w[r], xv, -zf * xc, magic), acc[r]);
             }
         }
+        if (slot == per_tile - 1) {
+            // tile complete: reduce across lanes and apply the epilogue
+            const int row0 = t * R;
 #pragma unroll
-        for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
-
-        if constexpr (EPI == kW4Swiglu) {
-            // Tile = R/2 gate rows then the matching R/2 up rows (packed at load time).
-            // silu(g) * u as in src/op/kernels/cuda/swiglu_kernel.cu:11-12.
-            if (lane < R / 2) {
-                float g = acc[0], u = acc[R / 2];
+            for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
+            if constexpr (EPI == kW4Swiglu) {
+                // Tile = R/2 gate rows then the matching R/2 up rows (packed at load time).
+                // silu(g) * u as in src/op/kernels/cuda/swiglu_kernel.cu:11-12.
+                if (lane < R / 2) {
+                    float g = acc[0], u = acc[R / 2];
 #pragma unroll
-                for (int j = 1; j < R / 2; ++j)
-                    if (lane == j) { g = acc[j]; u = acc[R / 2 + j]; }
-                const float silu = g * 1.0f / (1.0f + expf(-g));
-                a.y[t * (R / 2) + lane] = silu * u;
-            }
-        } else {
-            if (lane < R) {
-                float v = acc[0];
+                    for (int j = 1; j < R / 2; ++j)
+                        if (lane == j) { g = acc[j]; u = acc[R / 2 + j]; }
+                    const float silu = g * 1.0f / (1.0f + expf(-g));
+                    a.y[t * (R / 2) + lane] = silu * u;
+                }
+            } else {
+                if (lane < R) {
+                    float v = acc[0];
 #pragma unroll
-                for (int j = 1; j < R; ++j)
-                    if (lane == j) v = acc[j];
-                const int row = row0 + lane;
-                if (row < N) {
-                    if constexpr (EPI == kW4Residual) v = a.residual[row] + v;
-                    a.y[row] = v;
+                    for (int j = 1; j < R; ++j)
+                        if (lane == j) v = acc[j];
+                    const int row = row0 + lane;
+                    if (row < N) {
+                        if constexpr (EPI == kW4Residual) v = a.residual[row] + v;
+                        a.y[row] = v;
+                    }
                 }
             }
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r] = 0.0f;
         }
+        cur = nxt;
     }
 }
 
 template <int R, int EPI>
 cudaError_t launch_t(const W4Args& a, int num_sms, cudaStream_t stream, bool pdl) {
     auto kern = w4g128_gemv_kernel<R, EPI>;
-    const int smem = a.K * 4;
-    if (smem > 48 * 1024) {
-        // Opt in once per device to the larger dynamic shared memory this K needs.
-        static int configured[64] = {};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 0 || dev >= 64 || smem > configured[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(
-                kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-            if (e != cudaSuccess) return e;
-            if (dev >= 0 && dev < 64) configured[dev] = 227 * 1024;
-        }
+    const int smem = a.K * 4 + (a.K / 32) * 4;  // x (pre-scaled) + per-chunk sums
+    if (smem > 46 * 1024) {  // static shared memory also counts against the 48 KiB default
+        // Opt in to exactly the dynamic shared memory this K needs (the limit counts
+        // the kernel's static shared memory too).
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
     }
     const int tiles = (a.N + R - 1) / R;
     cudaLaunchConfig_t cfg = {};

@@ -13,7 +13,9 @@ constexpr int kW4TileRows = 4;
 
 struct W4Args {
     const float* x;          // [K] input (the raw hidden state when norm_w is set)
-    const float* norm_w;     // optional RMSNorm weight [K] applied to x first
+    const float* x_add;      // optional [K]: the input is x + x_add (residual fused into the prologue)
+    float* x_sum_out;        // optional [K]: CTA 0 stores x + x_add here (the new residual stream)
+    const float* norm_w;     // optional RMSNorm weight [K] applied to the (summed) input
     float eps;
     const uint8_t* qw;       // [N, K/2], 16-byte aligned
     const float* scales;     // [N, K/128]
@@ -22,6 +24,7 @@ struct W4Args {
     const float* residual;   // residual epilogue: y = residual + W x
     int N, K;                // K % 128 == 0
     int prefetch;            // issue an L2 bulk prefetch of each warp's first tile
+    uint32_t magic = 0x4B000000u;  // float 2^23 bits, passed at run time (keeps one LOP3 per weight)
 };
 
 cudaError_t w4g128_gemv_launch(const W4Args& a, int epilogue, int num_sms, cudaStream_t stream,

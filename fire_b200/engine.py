@@ -1,0 +1,166 @@
+"""Python face of the C++ Qwen3 decode engine (include/fire_b200_qwen3.h).
+
+Mirrors Fire's ``Model`` contract (include/Fire/model/model.h:22-52): ``prepare``,
+``forward(token_id, pos, logits)``, ``reset``, plus the greedy loops. Weights come
+from a ``.fire`` file (``Qwen3Engine.open``) or from named arrays / CUDA tensors
+(``Qwen3Engine(profile, tensors)``), e.g. a synthetic checkpoint from
+``fire_b200.synth``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Dict, Optional, Sequence
+
+import numpy as np
+
+from . import _engine_sigs as E
+from . import _native as N
+from .profiles import Qwen3Profile
+
+
+def _profile(p: Qwen3Profile) -> E.Profile:
+    return E.Profile(p.vocab_size, p.max_seq_len, p.hidden_size, p.intermediate_size, p.num_layers,
+                     p.num_attention_heads, p.num_kv_heads, p.head_dim, p.rms_norm_eps, p.rope_theta)
+
+
+def _options(tp_rank, tp_size, nccl_id, use_graph, pdl, keep) -> E.Options:
+    idp = None
+    if nccl_id is not None:
+        buf = C.create_string_buffer(bytes(nccl_id), 128)
+        keep.append(buf)
+        idp = C.cast(buf, C.c_void_p)
+    return E.Options(tp_rank, tp_size, idp, 1 if use_graph else 0, 1 if pdl else 0)
+
+
+def _descriptor(name: str, a, keep) -> E.Tensor:
+    try:
+        import torch
+    except ImportError:  # pragma: no cover
+        torch = None
+    if torch is not None and isinstance(a, torch.Tensor):
+        a = a.contiguous()
+        keep.append(a)
+        dt = {torch.float32: N.F32, torch.bfloat16: N.BF16, torch.int16: N.BF16, torch.uint8: 2}[a.dtype]
+        shape = tuple(a.shape)
+        ptr, dev = a.data_ptr(), 1 if a.is_cuda else 0
+    else:
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        dt = {np.dtype(np.float32): N.F32, np.dtype(np.uint16): N.BF16, np.dtype(np.uint8): 2}[a.dtype]
+        shape = a.shape
+        ptr, dev = a.ctypes.data, 0
+    nm = name.encode("ascii")
+    keep.append(nm)
+    s = (C.c_int64 * 2)(shape[0], shape[1] if len(shape) == 2 else 0)
+    return E.Tensor(nm, dt, len(shape), s, ptr, dev)
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    N.check(N.lib().fire_b200_nccl_unique_id(C.cast(buf, C.c_void_p)), "nccl unique id")
+    return buf.raw
+
+
+class Qwen3Engine:
+    def __init__(self, profile: Qwen3Profile, tensors: Optional[Dict[str, object]] = None, *, path: str = None,
+                 tp_rank: int = 0, tp_size: int = 1, nccl_id: Optional[bytes] = None, use_graph: bool = True,
+                 pdl: bool = True):
+        L = N.lib()
+        self.profile = profile
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        keep: list = []
+        prof = _profile(profile)
+        opts = _options(tp_rank, tp_size, nccl_id, use_graph, pdl, keep)
+        h = C.c_void_p()
+        if path is not None:
+            rc = L.fire_b200_qwen3_open(path.encode(), C.byref(prof), C.byref(opts), C.byref(h))
+        else:
+            descs = [_descriptor(n, a, keep) for n, a in tensors.items()]
+            arr = (E.Tensor * len(descs))(*descs)
+            rc = L.fire_b200_qwen3_create(C.byref(prof), arr, len(descs), C.byref(opts), C.byref(h))
+        if rc != N.OK:
+            raise N.FireB200Error(rc, "qwen3 create: " + L.fire_b200_qwen3_last_error().decode())
+        self._h = h
+        self._L = L
+
+    @classmethod
+    def open(cls, path: str, profile: Qwen3Profile, **kw) -> "Qwen3Engine":
+        return cls(profile, path=path, **kw)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._L.fire_b200_qwen3_destroy(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def prepare(self, capacity: int) -> None:
+        N.check(self._L.fire_b200_qwen3_prepare(self._h, capacity), "prepare")
+
+    def forward(self, token: int, pos: int, logits=None, stream=None) -> None:
+        """Model::forward; `logits` (CUDA float32 [vocab]) receives a copy when given."""
+        ptr = None if logits is None else logits.data_ptr()
+        N.check(self._L.fire_b200_qwen3_forward(self._h, int(token), int(pos), ptr, N.stream_handle(stream)),
+                "forward")
+
+    def generate(self, first_token: int, steps: int, out=None, stream=None):
+        """Device-side greedy loop; returns a CUDA int32 tensor [steps] (asynchronous)."""
+        import torch
+
+        if out is None:
+            out = torch.empty(steps, dtype=torch.int32, device="cuda")
+        N.check(self._L.fire_b200_qwen3_generate(self._h, int(first_token), int(steps), out.data_ptr(),
+                                                 N.stream_handle(stream)), "generate")
+        return out
+
+    def generate_host(self, prompt: Sequence[int], steps: int, stream=None) -> np.ndarray:
+        """The reference's host loop: per token H2D + step + D2H + synchronise."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(steps, np.int32)
+        N.check(self._L.fire_b200_qwen3_generate_host(self._h, p.ctypes.data, p.size, int(steps), out.ctypes.data,
+                                                      N.stream_handle(stream)), "generate_host")
+        return out
+
+    def reset(self) -> None:
+        N.check(self._L.fire_b200_qwen3_reset(self._h), "reset")
+
+    def truncate(self, length: int) -> None:
+        N.check(self._L.fire_b200_qwen3_truncate(self._h, int(length)), "truncate")
+
+    @property
+    def length(self) -> int:
+        return self._L.fire_b200_qwen3_length(self._h)
+
+    def logits_ptr(self) -> int:
+        return self._L.fire_b200_qwen3_logits(self._h)
+
+    @property
+    def kernels_per_step(self) -> int:
+        return self._L.fire_b200_qwen3_kernels_per_step(self._h)
+
+    @property
+    def step_weight_bytes(self) -> int:
+        return int(self._L.fire_b200_qwen3_step_weight_bytes(self._h))
+
+
+def smoke_decode() -> None:
+    """Tiny Qwen3 on cuda:0: three forwards against the oracle, then a greedy check."""
+    import torch
+
+    from oracle import oracle as O
+
+    from . import synth
+    from .profiles import TINY
+
+    w = synth.generate(TINY, "int4", seed=1)
+    eng = Qwen3Engine(TINY, w)
+    eng.prepare(16)
+    ref = O.Qwen3Oracle(TINY, w, capacity=16)
+    logits = torch.empty(TINY.vocab_size, device="cuda")
+    for pos, tok in enumerate([3, 141, 592]):
+        eng.forward(tok, pos, logits)
+        torch.cuda.synchronize()
+        r = ref.forward(tok, pos)
+        rel = float(np.linalg.norm(logits.cpu().numpy() - r) / np.linalg.norm(r))
+        assert rel < 1e-4, f"engine logits rel-L2 {rel} at pos {pos}"
+    eng.close()

@@ -41,8 +41,9 @@ enum {
     FIRE_B200_ERR_NOMEM = -6        /* device memory reservation failed */
 };
 
-/* Weight element types for dense (non-quantised) weights and embedding tables. */
-enum { FIRE_B200_F32 = 0, FIRE_B200_BF16 = 1 };
+/* Element types: dense weights and embedding tables (F32, BF16); packed INT4 and
+ * zero points (U8). */
+enum { FIRE_B200_F32 = 0, FIRE_B200_BF16 = 1, FIRE_B200_U8 = 2 };
 
 int fire_b200_abi_version(void);
 const char* fire_b200_status_string(int status);

@@ -1,0 +1,99 @@
+/*
+ * fire_b200_qwen3.h - C ABI of the Qwen3 single-token decode engine (B200, sm_100a).
+ *
+ * The engine is the GPU body behind Fire's Model / Qwen3Model / Qwen3Loader
+ * (include/Fire/model/model.h:22-52, src/model/qwen.cpp:30-311,
+ * src/model/qwen_loader.cpp:123-223): one handle serves one sequence on the current
+ * CUDA device, or one tensor-parallel rank of it. Status codes and stream
+ * conventions are those of fire_b200.h.
+ */
+#ifndef FIRE_B200_QWEN3_H
+#define FIRE_B200_QWEN3_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "fire_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct fire_b200_qwen3 fire_b200_qwen3; /* opaque engine handle */
+
+/* Architecture constants: Qwen3Profile (include/Fire/model/model_weights.h:108-137). */
+typedef struct {
+    int vocab_size, max_seq_len, hidden_size, intermediate_size, num_layers;
+    int num_attention_heads, num_kv_heads, head_dim;
+    float rms_norm_eps, rope_theta;
+} fire_b200_qwen3_profile;
+
+/* One checkpoint tensor, named as Fire's exporter names it (tools/export_qwen3.py:268-395):
+ * "tok_embeddings.weight", "layers.{i}.attention.wq.qweight|scales|zero_points", ...,
+ * "norm.weight", "output.weight" or "output.qweight|scales|zero_points". */
+typedef struct {
+    const char* name;
+    int dtype;         /* FIRE_B200_F32, FIRE_B200_BF16 or FIRE_B200_U8 */
+    int ndim;          /* 1 or 2 */
+    int64_t shape[2];
+    const void* data;  /* host memory, or device memory of the current device */
+    int on_device;
+} fire_b200_tensor;
+
+typedef struct {
+    int tp_rank;          /* 0 .. tp_size-1 */
+    int tp_size;          /* 1 = single GPU; >1 = tensor parallel, one process per GPU */
+    const void* nccl_id;  /* 128-byte NCCL unique id, the same on every rank (tp_size > 1) */
+    int use_graph;        /* capture each decode step in a CUDA graph (recommended: 1) */
+    int pdl;              /* programmatic dependent launch between kernels (recommended: 1) */
+} fire_b200_qwen3_options;
+
+/* A new NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */
+int fire_b200_nccl_unique_id(void* id128);
+
+/* Import weights (INT4 group-128 projections; FP32/BF16/INT4 LM head; FP32/BF16
+ * embedding) into device memory and build the engine: Qwen3Loader::load_weights +
+ * Qwen3Model::create. Tensor parallel ranks keep only their shard. */
+int fire_b200_qwen3_create(const fire_b200_qwen3_profile* profile, const fire_b200_tensor* tensors, int count,
+                           const fire_b200_qwen3_options* options, fire_b200_qwen3** out);
+/* The same from a .fire v1/v2 file (Qwen3Loader::open, src/model/qwen_loader.cpp:12-17). */
+int fire_b200_qwen3_open(const char* fire_path, const fire_b200_qwen3_profile* profile,
+                         const fire_b200_qwen3_options* options, fire_b200_qwen3** out);
+/* Message of the last failed create/open on this thread ("" if none). */
+const char* fire_b200_qwen3_last_error(void);
+
+/* Model::prepare: runtime buffers, KV cache and RoPE caches for 1 <= capacity <= max_seq_len;
+ * starts an empty sequence. Synchronises the device. */
+int fire_b200_qwen3_prepare(fire_b200_qwen3* m, int capacity);
+/* Model::forward: consume token_id at pos (must equal the current length); logits [vocab]
+ * FP32 land in the engine buffer (fire_b200_qwen3_logits) and, if non-NULL, in `logits`
+ * (device). Success advances the length by one. Asynchronous on `stream`. */
+int fire_b200_qwen3_forward(fire_b200_qwen3* m, int token_id, int pos, float* logits, void* stream);
+/* Greedy decode of `steps` tokens on the device from `first_token` at the current length:
+ * tokens_out (device int32 [steps]) receives the argmax ids (first index on ties); no host
+ * round trip between tokens. Advances the length by `steps`. */
+int fire_b200_qwen3_generate(fire_b200_qwen3* m, int first_token, int steps, int32_t* tokens_out, void* stream);
+/* The reference's host decode loop (demo/qwen_chat.cpp:231-294 + ArgmaxSampler): prompt tokens
+ * one by one, then per generated token an H2D copy of its input id, one step, a D2H copy of
+ * the sampled id and a stream synchronisation. prompt/out are host arrays; out gets `steps` ids. */
+int fire_b200_qwen3_generate_host(fire_b200_qwen3* m, const int32_t* prompt, int n_prompt, int steps,
+                                  int32_t* out, void* stream);
+/* Model::reset: empty the sequence, keep weights and capacity. */
+int fire_b200_qwen3_reset(fire_b200_qwen3* m);
+/* Shorten the sequence to `length` tokens (0 <= length <= current length), keeping the KV
+ * cache of the kept prefix, so a shared prompt can be decoded from again. */
+int fire_b200_qwen3_truncate(fire_b200_qwen3* m, int length);
+int fire_b200_qwen3_length(const fire_b200_qwen3* m);
+/* Device pointer to the last logits [vocab] (full vocabulary on every rank). */
+const float* fire_b200_qwen3_logits(const fire_b200_qwen3* m);
+/* Kernels of this library one sampled decode step launches (CUDA graph nodes). */
+int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m);
+/* Weight bytes one decode step reads on this rank (projections, head, norms, one
+ * embedding row): the numerator of the HBM roofline. */
+uint64_t fire_b200_qwen3_step_weight_bytes(const fire_b200_qwen3* m);
+void fire_b200_qwen3_destroy(fire_b200_qwen3* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FIRE_B200_QWEN3_H */

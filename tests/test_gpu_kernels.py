@@ -251,7 +251,8 @@ def test_rope_cache_and_rotation(cuda, head, max_seq, qh, kh, theta):
     tol = 2e-6 + pos * 1e-7
     ang = pos * np.power(np.float64(theta), -2.0 * np.arange(head // 2)[None, :] / head)
     assert np.all(np.abs(s - np.sin(ang)) <= tol) and np.all(np.abs(c - np.cos(ang)) <= tol)
-    assert np.mean(s == s_ref) > 0.99 and np.mean(c == c_ref) > 0.99  # same FP32 rounding almost always
+    # against the oracle (glibc powf/sinf/cosf) within the same bound
+    assert np.all(np.abs(s - s_ref) <= tol) and np.all(np.abs(c - c_ref) <= tol)
     rng = np.random.default_rng(head)
     q = rng.normal(0, 1, (qh, head)).astype(np.float32)
     k = rng.normal(0, 1, (kh, head)).astype(np.float32)
