@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="fire_b200", choices=["fire_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # profiling knobs (defaults are the measured workload)
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled once")
+    ap.add_argument("--gen", type=int, default=GEN, help="greedy tokens per step")
     return ap.parse_args()
 
 
@@ -282,7 +285,9 @@ def run_ours(args):
     torch.cuda.empty_cache()
     eng.prepare(CAPACITY)
     stream = torch.cuda.Stream()
-    prompt = np.random.default_rng(0).integers(0, p.vocab_size, PROMPT)
+    n_prompt, n_gen = args.prompt, args.gen
+    assert 1 <= n_prompt and n_prompt + n_gen - 1 <= CAPACITY
+    prompt = np.random.default_rng(0).integers(0, p.vocab_size, n_prompt)
     with torch.cuda.stream(stream):
         for i, t in enumerate(prompt[:-1]):
             eng.forward(int(t), i, stream=stream)
@@ -294,8 +299,8 @@ def run_ours(args):
             dist.barrier()
 
     def step():
-        eng.truncate(PROMPT - 1)
-        return eng.generate(first, GEN, stream=stream)
+        eng.truncate(n_prompt - 1)
+        return eng.generate(first, n_gen, stream=stream)
 
     for _ in range(args.warmup):
         toks = step()
@@ -314,8 +319,8 @@ def run_ours(args):
     ms = e0.elapsed_time(e1)
     same = toks.cpu().tolist() == ref_tokens
     # end to end through the C ABI with host buffers (reference-style loop)
-    eng.truncate(PROMPT - 1)
-    eng.generate_host([first], GEN, stream=stream)  # warm
+    eng.truncate(n_prompt - 1)
+    eng.generate_host([first], n_gen, stream=stream)  # warm
     barrier()
     torch.cuda.synchronize()
     h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -323,8 +328,8 @@ def run_ours(args):
     h0.record(stream)
     e2e_tokens = None
     for _ in range(args.steps):
-        eng.truncate(PROMPT - 1)
-        e2e_tokens = eng.generate_host([first], GEN, stream=stream)
+        eng.truncate(n_prompt - 1)
+        e2e_tokens = eng.generate_host([first], n_gen, stream=stream)
     h1.record(stream)
     torch.cuda.synchronize()
     wall_e2e = time.perf_counter() - t0
@@ -347,10 +352,10 @@ def run_ours(args):
     if rank == 0:
         pk = peaks()
         peak = float(pk.get("hbm_gbs", 6650.0))
-        tok_s = GEN * args.steps / (ms / 1e3)
-        tok_s_e2e = GEN * args.steps / (ms_e2e / 1e3)
+        tok_s = n_gen * args.steps / (ms / 1e3)
+        tok_s_e2e = n_gen * args.steps / (ms_e2e / 1e3)
         step_bytes = eng.step_weight_bytes  # per GPU per token
-        per_tok_s = (ms / 1e3) / (GEN * args.steps)
+        per_tok_s = (ms / 1e3) / (n_gen * args.steps)
         traffic = None
         try:
             traffic = json.load(open(os.path.join(ROOT, "profiles", "w4_gemv_traffic.json"))).get(
@@ -363,11 +368,11 @@ def run_ours(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "qwen3-8b-w4-decode-ctx2048", "model": "Qwen3-8B (random init)",
                        "layout": "mixed: INT4 g128 projections, BF16 embedding/head, FP32 norms/activations/KV",
-                       "prompt": PROMPT, "generated_per_step": GEN, "context": CAPACITY,
+                       "prompt": n_prompt, "generated_per_step": n_gen, "context": n_prompt + n_gen,
                        "parallelism": f"tp{world}", "l2": "weights 4.99 GB/token > 126 MB L2 (no flush needed)"},
-            "e2e": {"value": tok_s_e2e, "unit": "tok/s", "h2d_bytes_per_step": 16 * GEN,
-                    "d2h_bytes_per_step": 4 * GEN},
-            "gpu_launches": (eng.kernels_per_step * GEN + 1) * args.steps,
+            "e2e": {"value": tok_s_e2e, "unit": "tok/s", "h2d_bytes_per_step": 16 * n_gen,
+                    "d2h_bytes_per_step": 4 * n_gen},
+            "gpu_launches": (eng.kernels_per_step * n_gen + 1) * args.steps,
             "roofline": {"bound": "hbm", "kernel": "w4g128_gemv_kernel", "achieved": w4_bytes / (w4_us * 1e3),
                          "peak": peak, "unit": "GB/s", "frac": w4_bytes / (w4_us * 1e3) / peak,
                          "traffic": traffic, "bytes_per_launch": w4_bytes, "us_per_launch": w4_us,
