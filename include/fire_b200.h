@@ -106,6 +106,22 @@ int fire_b200_mha_decode(const float* q, const float* key_cache, const float* va
                          int kv_heads, int head_dim, int layer, int pos, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* The same attention for callers that cannot allocate device memory or pass a workspace:
+ * e.g. a plug-in behind an interface that hands over only its tensors (like Fire's
+ * MHAKernel: q, caches, score, output), or a program whose device memory is fixed at
+ * start-up so nothing may be allocated later. No counterpart in the reference: Fire's
+ * kernel keeps its scores in the caller's `score` tensor and allocates nothing else.
+ * Its scratch is a 4 MiB array inside the library (held in every GPU's memory from
+ * library load to process exit), so it calls no allocator; shapes whose scratch,
+ * fire_b200_mha_workspace_bytes(q_heads, kv_heads, head_dim, capacity), exceeds
+ * 4 MiB are rejected with FIRE_B200_ERR_UNSUPPORTED (e.g. 32 q heads of dim 128 fit up
+ * to capacity 16128). The first call on each device looks the array's device address
+ * up (make that first call before any stream capture). All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller. */
+int fire_b200_mha_decode_noalloc(const float* q, const float* key_cache, const float* value_cache,
+                                 float* score, float* out, int layers, int capacity, int q_heads,
+                                 int kv_heads, int head_dim, int layer, int pos, void* stream);
+
 /* Embedding row gather, BF16 rows widened to FP32: out[i, :] = table[tokens[i], :].
  * Replaces kernel::emb_kernel_cu (src/op/kernels/cuda/emb_kernel.cu:64-86). tokens are
  * device int32 [count]; out-of-range tokens leave their output row untouched. */
