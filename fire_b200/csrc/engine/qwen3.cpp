@@ -388,25 +388,15 @@ int Qwen3Engine::enqueue_step(cudaStream_t s, bool sample) {
         a.y = qkv_;
         a.prefetch = 1;
         FB_CK(w4g128_gemv_launch(a, kW4Store, sms_, s, pdl));
-        // q_norm / k_norm, RoPE, KV write (qwen.cpp:222-240)
-        QkRopeArgs r{};
-        r.qkv = qkv_;
-        r.q_norm = L.q_norm;
-        r.k_norm = L.k_norm;
-        r.rope_sin = rope_sin_;
-        r.rope_cos = rope_cos_;
-        r.q_out = q_rot_;
-        r.key_cache = kcache_ + kv_layer;
-        r.value_cache = vcache_ + kv_layer;
-        r.state = state_;
-        r.q_heads = hq_;
-        r.kv_heads = hkv_;
-        r.capacity = capacity_;
-        r.eps = d_.eps;
-        FB_CK(qk_norm_rope_kv_launch(r, s, pdl));
-        // attention (qwen.cpp:242-247)
+        // q_norm / k_norm, RoPE, KV write (qwen.cpp:222-240) fused into attention (qwen.cpp:242-247)
         AttnArgs at{};
-        at.q = q_rot_;
+        at.q = nullptr;
+        at.qkv = qkv_;
+        at.q_norm = L.q_norm;
+        at.k_norm = L.k_norm;
+        at.rope_sin = rope_sin_;
+        at.rope_cos = rope_cos_;
+        at.eps = d_.eps;
         at.key_cache = kcache_ + kv_layer;
         at.value_cache = vcache_ + kv_layer;
         at.out = attn_out_;
@@ -519,7 +509,7 @@ int Qwen3Engine::launch_step(cudaStream_t s, bool sample) {
     return enqueue_step(s, sample);
 }
 
-int Qwen3Engine::kernels_per_step() const { return 6 * d_.layers + 3 + (tp_ > 1 ? 1 : 0); }
+int Qwen3Engine::kernels_per_step() const { return 5 * d_.layers + 3 + (tp_ > 1 ? 1 : 0); }
 
 int Qwen3Engine::forward(int token, int pos, float* logits_out, cudaStream_t s) {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;

@@ -70,4 +70,39 @@ __device__ __forceinline__ float load_input(const float* x, const float* x_add, 
     return v;
 }
 
+// a' = a*cos - b*sin, b' = a*sin + b*cos with every product rounded separately, as
+// Fire's CPU RoPE computes it (src/op/kernels/cpu/rope_kernel.cpp:38-49).
+__device__ __forceinline__ void rope_rotate(float& a, float& b, float fcr, float fci) {
+    const float a0 = a, b0 = b;
+    a = __fsub_rn(__fmul_rn(a0, fcr), __fmul_rn(b0, fci));
+    b = __fadd_rn(__fmul_rn(a0, fci), __fmul_rn(b0, fcr));
+}
+
+// One 128-wide head held by a warp, lane l owning dims 4l..4l+3: per-head RMSNorm with
+// weight nw (rmsnorm_kernel.cpp:41-67) then half-split RoPE at the cache rows sin_row /
+// cos_row [64] (rope_kernel.cpp:26-52); the RoPE partner of lane l is lane l^16.
+__device__ __forceinline__ void head_norm_rope(float (&v)[4], const float* nw, const float* sin_row,
+                                               const float* cos_row, float eps) {
+    const int lane = threadIdx.x & 31;
+    float ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], v[3] * v[3])));
+    ss = warp_sum(ss);
+    const float scale = 1.0f / sqrtf(ss / 128.0f + eps);
+    const float4 w4 = reinterpret_cast<const float4*>(nw)[lane];
+    v[0] = v[0] * w4.x * scale;
+    v[1] = v[1] * w4.y * scale;
+    v[2] = v[2] * w4.z * scale;
+    v[3] = v[3] * w4.w * scale;
+    const float4 s4 = reinterpret_cast<const float4*>(sin_row)[lane & 15];
+    const float4 c4 = reinterpret_cast<const float4*>(cos_row)[lane & 15];
+    const float sn[4] = {s4.x, s4.y, s4.z, s4.w}, cs[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[j], 16);
+        float a0, b0;
+        if (lane < 16) { a0 = v[j]; b0 = other; } else { a0 = other; b0 = v[j]; }
+        rope_rotate(a0, b0, cs[j], sn[j]);
+        v[j] = lane < 16 ? a0 : b0;
+    }
+}
+
 }  // namespace fb

@@ -64,12 +64,7 @@ __global__ void rope_cache_kernel(int head, int max_seq, float theta, float* __r
     }
 }
 
-__device__ __forceinline__ void rotate(float& a, float& b, float fcr, float fci) {
-    // a' = a*cos - b*sin, b' = a*sin + b*cos, each product rounded (rope_kernel.cpp:38-49)
-    const float a0 = a, b0 = b;
-    a = __fsub_rn(__fmul_rn(a0, fcr), __fmul_rn(b0, fci));
-    b = __fadd_rn(__fmul_rn(a0, fci), __fmul_rn(b0, fcr));
-}
+__device__ __forceinline__ void rotate(float& a, float& b, float fcr, float fci) { rope_rotate(a, b, fcr, fci); }
 
 // Half-split rotation of q [q_heads, head] and k [k_heads, head] at `pos`;
 // one thread per (head, pair), q heads first.

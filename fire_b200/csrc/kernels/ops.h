@@ -36,6 +36,16 @@ struct AttnArgs {
     int pos;
     int q_heads, kv_heads, hd, capacity, max_chunks;
     float scale;             // 1/sqrt(hd)
+    // Fused q/k-norm + RoPE + KV write (decode engine, hd 128): when qkv is set, q, k
+    // and v of the current token come raw from qkv = [q | k | v] (all heads of this
+    // rank); each CTA normalises and rotates its q heads, and the CTA whose chunk holds
+    // `pos` rotates k and writes k and v into the cache (src/model/qwen.cpp:222-240).
+    const float* qkv = nullptr;
+    const float* q_norm = nullptr;
+    const float* k_norm = nullptr;
+    const float* rope_sin = nullptr;  // [capacity, 64]
+    const float* rope_cos = nullptr;
+    float eps = 0.f;
 };
 
 constexpr int kAttnChunk = 64;  // keys per split
