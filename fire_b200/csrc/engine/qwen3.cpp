@@ -362,7 +362,8 @@ int Qwen3Engine::enqueue_step(cudaStream_t s, bool sample) {
         const int r = nccl().AllReduce(buf, buf, size_t(H), kNcclFloat32, 0, comm_, s);
         return r == 0 ? 0 : FIRE_B200_ERR_STATE;
     };
-    auto mat = [](W4Args& a, const W4Mat& m) {
+    auto mat = [this](W4Args& a, const W4Mat& m) {
+        a.err = &state_->error;
         a.qw = m.qw;
         a.scales = m.s;
         a.zeros = m.z;

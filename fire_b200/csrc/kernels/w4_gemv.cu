@@ -25,6 +25,9 @@
 //    the producer of x.
 #include "common.cuh"
 #include "w4_gemv.h"
+
+#include <cstdlib>
+#include <cstring>
 #include "w4_gemv_common.cuh"
 #include "w4_gemv_spec.cuh"
 
@@ -177,6 +180,13 @@ cudaError_t w4g128_gemv_launch(const W4Args& a, int epi, int num_sms, cudaStream
                                bool pdl) {
     // K-specialised kernels (w4_gemv_spec.cuh) cover the decode shapes; R = 4 rows per
     // lane group when there are enough tiles to fill every warp of the grid, else R = 2.
+    // FIRE_B200_W4_PATH=mma selects the integer tensor-core kernel (w4_mma.cu) where it
+    // applies (N % 16 == 0); the FP32 streaming kernels below are the default.
+    static const bool mma = [] {
+        const char* v = std::getenv("FIRE_B200_W4_PATH");
+        return v != nullptr && std::strcmp(v, "mma") == 0;
+    }();
+    if (mma && w4_mma_supported(a)) return w4_mma_launch(a, epi, num_sms, stream, pdl);
     cudaError_t err = cudaSuccess;
     if (epi == kW4Swiglu) {
         if (a.N % kW4TileRows == 0 && a.N >= kW4TileRows && w4_spec_swiglu(a, num_sms, stream, pdl, &err))

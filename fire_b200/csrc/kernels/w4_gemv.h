@@ -25,10 +25,15 @@ struct W4Args {
     int N, K;                // K % 128 == 0
     int prefetch;            // issue an L2 bulk prefetch of each warp's first tile
     uint32_t magic = 0x4B000000u;  // float 2^23 bits, passed at run time (keeps one LOP3 per weight)
+    int* err = nullptr;      // optional device word set non-zero if a bounded wait gives up
 };
 
 cudaError_t w4g128_gemv_launch(const W4Args& a, int epilogue, int num_sms, cudaStream_t stream,
                                bool pdl);
+// Tensor-core path (w4_mma.cu): exact u8 x s8 integer MMAs on fixed-point digits of x.
+bool w4_mma_supported(const W4Args& a);
+cudaError_t w4_mma_launch(const W4Args& a, int epilogue, int num_sms, cudaStream_t stream, bool pdl);
+
 cudaError_t w4_linear_generic_launch(const float* x, const uint8_t* qw, const float* scales,
                                      const uint8_t* zeros, float* y, int rows, int N, int K,
                                      int group, int num_sms, cudaStream_t stream);
