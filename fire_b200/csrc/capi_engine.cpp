@@ -140,6 +140,9 @@ int fire_b200_qwen3_truncate(fire_b200_qwen3* m, int length) {
 int fire_b200_qwen3_length(const fire_b200_qwen3* m) { return m ? m->e->length() : -1; }
 const float* fire_b200_qwen3_logits(const fire_b200_qwen3* m) { return m ? m->e->logits() : nullptr; }
 int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m) { return m ? m->e->kernels_per_step() : 0; }
+int64_t fire_b200_qwen3_stack_trace(const fire_b200_qwen3* m, uint64_t* out, int64_t capacity_words) {
+    return m ? m->e->stack_trace(out, capacity_words) : 0;
+}
 uint64_t fire_b200_qwen3_step_weight_bytes(const fire_b200_qwen3* m) {
     return m ? static_cast<uint64_t>(m->e->step_weight_bytes()) : 0;
 }

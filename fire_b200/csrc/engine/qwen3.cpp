@@ -1,6 +1,8 @@
 #include "engine/qwen3.h"
 
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <unordered_map>
 
@@ -100,6 +102,17 @@ int Qwen3Engine::create(const Qwen3Dims& d, const std::vector<TensorSrc>& tensor
     e->f_ = d.inter / t;
     e->v_ = d.vocab / t;
     e->v_off_ = e->rank_ * e->v_;
+    // the persistent layer-stack kernel serves tensor-parallel size 1 when the shapes fit
+    // (FIRE_B200_LAYER_STACK=0 selects the per-op kernels)
+    if (t == 1) {
+        const char* env = std::getenv("FIRE_B200_LAYER_STACK");
+        if (env == nullptr || std::strcmp(env, "0") != 0) {
+            StackArgs probe = e->stack_template(d.max_seq);
+            e->stack_ = stack_plan(&probe, e->sms_);
+            const char* tr = std::getenv("FIRE_B200_STACK_TRACE");
+            e->stack_trace_on_ = e->stack_ && tr != nullptr && std::strcmp(tr, "1") == 0;
+        }
+    }
     e->weight_arena_.reset(new DeviceArena(e->device_));
     e->runtime_arena_.reset(new DeviceArena(e->device_));
     const int rc = e->import_weights(tensors, err);
@@ -163,9 +176,11 @@ int Qwen3Engine::import_weights(const std::vector<TensorSrc>& tensors, std::stri
         return pad256(size_t(n) * k / 2) + pad256(size_t(n) * (k / 128) * 4) + pad256(size_t(n) * (k / 128));
     };
     size_t total = pad256(size_t(V) * H * esize(emb->dtype)) + pad256(size_t(H) * 4);
-    const size_t per_layer = w4_bytes(q_ + 2 * kv_, H) + w4_bytes(H, q_) + w4_bytes(2 * f_, H) + w4_bytes(H, f_) +
+    auto mat_bytes = [&](int n, int k) { return stack_ ? pad256(stack_items_bytes(n, k)) : w4_bytes(n, k); };
+    const size_t per_layer = mat_bytes(q_ + 2 * kv_, H) + mat_bytes(H, q_) + mat_bytes(2 * f_, H) + mat_bytes(H, f_) +
                              2 * pad256(size_t(H) * 4) + 2 * pad256(512);
     total += per_layer * L;
+    if (stack_) total += pad256(size_t(L) * sizeof(StackLayer));
     total += head_kind_ == 2 ? w4_bytes(v_, H) : pad256(size_t(v_) * H * (head_kind_ == 1 ? 2 : 4));
     FB_RC(weight_arena_->reserve(total + 4096));
     weight_bytes_ = total;
@@ -213,6 +228,35 @@ int Qwen3Engine::import_weights(const std::vector<TensorSrc>& tensors, std::stri
         }
     };
 
+    // layer-stack layout: each matrix is uploaded in the .fire layout to a scratch
+    // matrix, then repacked into items in the arena
+    W4Mat tmp{};
+    if (stack_) {
+        const size_t elems = std::max({size_t(q_ + 2 * kv_) * H, size_t(H) * q_, size_t(2 * f_) * H, size_t(H) * f_});
+        void *tq = nullptr, *ts = nullptr, *tz = nullptr;
+        if (cudaMalloc(&tq, elems / 2) != cudaSuccess || cudaMalloc(&ts, elems / 128 * 4) != cudaSuccess ||
+            cudaMalloc(&tz, elems / 128) != cudaSuccess) {
+            cudaFree(tq);
+            cudaFree(ts);
+            cudaFree(tz);
+            cudaStreamDestroy(s);
+            return fail(FIRE_B200_ERR_NOMEM, "no room for the repack scratch matrix");
+        }
+        tmp.qw = static_cast<uint8_t*>(tq);
+        tmp.s = static_cast<float*>(ts);
+        tmp.z = static_cast<uint8_t*>(tz);
+    }
+    auto pack = [&](uint8_t** out, int n, int k, int mode) {
+        *out = static_cast<uint8_t*>(alloc(stack_items_bytes(n, k)));
+        if (!*out) rc = FIRE_B200_ERR_NOMEM;
+        if (!rc) rc = static_cast<int>(stack_pack_launch(tmp.qw, tmp.s, tmp.z, n, k, mode, *out, s));
+    };
+    auto as_tmp = [&](int n, int k) -> W4Mat& {
+        tmp.n = n;
+        tmp.k = k;
+        return tmp;
+    };
+
     emb_bf16_ = emb->dtype == kSrcBF16;
     embedding_ = whole(emb, size_t(V) * H * esize(emb->dtype));
     final_norm_ = static_cast<float*>(whole(S.get("norm.weight"), size_t(H) * 4));
@@ -225,6 +269,26 @@ int Qwen3Engine::import_weights(const std::vector<TensorSrc>& tensors, std::stri
         y.ffn_norm = static_cast<float*>(whole(S.get(p + "ffn_norm.weight"), size_t(H) * 4));
         y.q_norm = static_cast<float*>(whole(S.get(p + "attention.q_norm.weight"), 512));
         y.k_norm = static_cast<float*>(whole(S.get(p + "attention.k_norm.weight"), 512));
+        if (stack_) {
+            y.qkv.n = q_ + 2 * kv_, y.qkv.k = H;
+            y.o.n = H, y.o.k = q_;
+            y.gu.n = 2 * f_, y.gu.k = H;
+            y.down.n = H, y.down.k = f_;
+            W4Mat& a = as_tmp(q_ + 2 * kv_, H);
+            w4_copy(a, p + "attention.wq", H, rank_ * q_, q_, 0, H, 0, 1, 1);
+            if (!rc) w4_copy(a, p + "attention.wk", H, rank_ * kv_, kv_, 0, H, q_, 1, 1);
+            if (!rc) w4_copy(a, p + "attention.wv", H, rank_ * kv_, kv_, 0, H, q_ + kv_, 1, 1);
+            if (!rc) pack(&y.qkv_items, q_ + 2 * kv_, H, kPackRows);
+            if (!rc) w4_copy(as_tmp(H, q_), p + "attention.wo", Q, 0, H, rank_ * q_, q_, 0, 1, 1);
+            if (!rc) pack(&y.o_items, H, q_, kPackRows);
+            // gate rows then up rows; the repack interleaves them per item row tile
+            if (!rc) w4_copy(as_tmp(2 * f_, H), p + "feed_forward.w1", H, rank_ * f_, f_, 0, H, 0, 1, 1);
+            if (!rc) w4_copy(tmp, p + "feed_forward.w3", H, rank_ * f_, f_, 0, H, f_, 1, 1);
+            if (!rc) pack(&y.gu_items, 2 * f_, H, kPackGateUp);
+            if (!rc) w4_copy(as_tmp(H, f_), p + "feed_forward.w2", F, 0, H, rank_ * f_, f_, 0, 1, 1);
+            if (!rc) pack(&y.down_items, H, f_, kPackRows);
+            continue;
+        }
         // q/k/v: this rank's heads, concatenated
         w4_alloc(y.qkv, q_ + 2 * kv_, H);
         if (!rc) w4_copy(y.qkv, p + "attention.wq", H, rank_ * q_, q_, 0, H, 0, 1, 1);
@@ -252,8 +316,24 @@ int Qwen3Engine::import_weights(const std::vector<TensorSrc>& tensors, std::stri
             if (!rc) rc = copy2d(head_dense_, rb, head, size_t(v_off_) * rb, rb, rb, v_, s);
         }
     }
+    std::vector<StackLayer> host_layers;
+    if (!rc && stack_) {
+        for (const auto& y : layers_)
+            host_layers.push_back(StackLayer{y.attn_norm, y.ffn_norm, y.q_norm, y.k_norm, y.qkv_items, y.o_items,
+                                             y.gu_items, y.down_items});
+        stack_layers_ = static_cast<StackLayer*>(alloc(size_t(L) * sizeof(StackLayer)));
+        if (!stack_layers_) rc = FIRE_B200_ERR_NOMEM;
+        if (!rc)
+            rc = static_cast<int>(cudaMemcpyAsync(stack_layers_, host_layers.data(), size_t(L) * sizeof(StackLayer),
+                                                  cudaMemcpyHostToDevice, s));
+    }
     const cudaError_t se = cudaStreamSynchronize(s);
     cudaStreamDestroy(s);
+    if (tmp.qw) {
+        cudaFree(tmp.qw);
+        cudaFree(tmp.s);
+        cudaFree(tmp.z);
+    }
     if (rc) return fail(rc, rc == FIRE_B200_ERR_NOMEM ? "device weight reservation exhausted" : "weight upload failed");
     if (se != cudaSuccess) return static_cast<int>(se);
 
@@ -278,10 +358,19 @@ int Qwen3Engine::prepare(int capacity) {
     const size_t kv_elems = size_t(d_.layers) * capacity * kv_;
     const size_t attn_ws = attention_workspace_bytes(hq_, hkv_, 128, capacity);
     const size_t am_ws = argmax_workspace_bytes(kMaxSms);
+    StackArgs sa{};
+    size_t stack_bytes = 0;
+    if (stack_) {
+        sa = stack_template(capacity);
+        if (!stack_plan(&sa, sms_)) return FIRE_B200_ERR_UNSUPPORTED;
+        stack_trace_words_ = stack_trace_on_ ? size_t(sa.grid) * d_.layers * kStackPhases * kStackTraceSlots : 0;
+        stack_bytes = pad256(stack_trace_words_ * 8) + pad256(stack_sync_words(sa) * 4) + pad256(stack_kpart_floats(sa) * 4 + 4) +
+                      pad256(size_t(hq_) * sa.max_chunks * 128 * 4) + pad256(size_t(hq_) * sa.max_chunks * 2 * 4) + 1024;
+    }
     size_t total = 0;
     const size_t sizes[] = {256, size_t(H) * 4 * 5, size_t(q_ + 2 * kv_) * 4, size_t(q_) * 8, size_t(f_) * 4,
                             size_t(v_) * 4, size_t(d_.vocab) * 4, kv_elems * 8, size_t(capacity) * 64 * 8,
-                            attn_ws, am_ws, 256, 256 * size_t(tp_), size_t(capacity) * 4};
+                            attn_ws, am_ws, 256, 256 * size_t(tp_), size_t(capacity) * 4, stack_bytes};
     for (size_t sz : sizes) total += pad256(sz) + 256;
     FB_RC(runtime_arena_->reserve(total));
     auto A = [&](size_t b) { return runtime_arena_->alloc(b); };
@@ -309,6 +398,32 @@ int Qwen3Engine::prepare(int capacity) {
         !logits_ || !logits_full_ || !kcache_ || !vcache_ || !rope_sin_ || !rope_cos_ || !attn_ws_ || !argmax_ws_ ||
         !best_local_ || !best_all_ || !tokens_buf_)
         return FIRE_B200_ERR_NOMEM;
+    if (stack_) {
+        stack_sync_bytes_ = stack_sync_words(sa) * 4;
+        stack_sync_ = static_cast<unsigned*>(A(stack_sync_bytes_));
+        sa.kpart = static_cast<float*>(A(stack_kpart_floats(sa) * 4 + 4));
+        sa.attn_part = static_cast<float*>(A(size_t(hq_) * sa.max_chunks * 128 * 4));
+        sa.attn_ml = static_cast<float*>(A(size_t(hq_) * sa.max_chunks * 2 * 4));
+        if (!stack_sync_ || !sa.kpart || !sa.attn_part || !sa.attn_ml) return FIRE_B200_ERR_NOMEM;
+        sa.layers = stack_layers_;
+        sa.state = state_;
+        sa.hidden_buf = hidden_;
+        sa.attn_res = attn_res_;
+        sa.qkv = qkv_;
+        sa.attn_out = attn_out_;
+        sa.act = act_;
+        sa.kcache = kcache_;
+        sa.vcache = vcache_;
+        sa.rope_sin = rope_sin_;
+        sa.rope_cos = rope_cos_;
+        sa.sync = stack_sync_;
+        sa.trace = nullptr;
+        if (stack_trace_words_) {
+            sa.trace = static_cast<unsigned long long*>(A(stack_trace_words_ * 8));
+            if (!sa.trace) return FIRE_B200_ERR_NOMEM;
+        }
+        stack_args_ = sa;
+    }
     if (!host_state_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_state_), sizeof(DecodeState)));
     if (!host_token_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_token_), sizeof(int32_t)));
 
@@ -336,6 +451,17 @@ int Qwen3Engine::prepare(int capacity) {
 }
 
 int Qwen3Engine::capture(bool sample, cudaGraphExec_t* exec) {
+    for (int attempt = 0;; ++attempt) {
+        const int rc = capture_once(sample, exec);
+        // a runtime that cannot capture a cooperative launch gets a plain one (one CTA per
+        // SM is resident either way: the kernel's shared memory admits no second CTA)
+        if (rc == 0 || !stack_ || !stack_coop_ || attempt > 0) return rc;
+        (void)cudaGetLastError();
+        stack_coop_ = false;
+    }
+}
+
+int Qwen3Engine::capture_once(bool sample, cudaGraphExec_t* exec) {
     cudaStream_t cs;
     FB_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
     cudaGraph_t g = nullptr;
@@ -371,7 +497,20 @@ int Qwen3Engine::enqueue_step(cudaStream_t s, bool sample) {
         a.K = m.k;
     };
     FB_CK(embedding_launch(nullptr, 1, state_, embedding_, emb_bf16_, d_.vocab, H, hidden_, s, pdl));
-    for (int l = 0; l < d_.layers; ++l) {
+    if (stack_) {
+        FB_CK(cudaMemsetAsync(stack_sync_, 0, stack_sync_bytes_, s));
+        if (stack_args_.trace) FB_CK(cudaMemsetAsync(stack_args_.trace, 0, stack_trace_words_ * 8, s));
+        cudaError_t e = stack_launch(stack_args_, s, stack_coop_);
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (e != cudaSuccess && stack_coop_ && cudaStreamIsCapturing(s, &cs) == cudaSuccess &&
+            cs == cudaStreamCaptureStatusNone) {
+            (void)cudaGetLastError();
+            stack_coop_ = false;
+            e = stack_launch(stack_args_, s, false);
+        }
+        FB_CK(e);
+    }
+    for (int l = 0; l < (stack_ ? 0 : d_.layers); ++l) {
         const Layer& L = layers_[l];
         const size_t kv_layer = size_t(l) * capacity_ * kv_;
         // q/k/v = W_qkv . rmsnorm(h)   (qwen.cpp:196-217)
@@ -510,7 +649,36 @@ int Qwen3Engine::launch_step(cudaStream_t s, bool sample) {
     return enqueue_step(s, sample);
 }
 
-int Qwen3Engine::kernels_per_step() const { return 5 * d_.layers + 3 + (tp_ > 1 ? 1 : 0); }
+int Qwen3Engine::kernels_per_step() const {
+    if (stack_) return 4;  // embedding, layer stack, LM head, argmax
+    return 5 * d_.layers + 3 + (tp_ > 1 ? 1 : 0);
+}
+
+int64_t Qwen3Engine::stack_trace(uint64_t* host_out, int64_t capacity_words) const {
+    if (!stack_args_.trace || !stack_trace_words_) return 0;
+    const int64_t n = static_cast<int64_t>(stack_trace_words_);
+    if (host_out && capacity_words > 0) {
+        const size_t m = static_cast<size_t>(capacity_words < n ? capacity_words : n);
+        if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+        if (cudaMemcpy(host_out, stack_args_.trace, m * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    }
+    return n;
+}
+
+StackArgs Qwen3Engine::stack_template(int capacity) const {
+    StackArgs a{};
+    a.L = d_.layers;
+    a.hidden = d_.hidden;
+    a.q_dim = q_;
+    a.kv_dim = kv_;
+    a.inter = f_;
+    a.q_heads = hq_;
+    a.kv_heads = hkv_;
+    a.eps = d_.eps;
+    a.scale = 1.0f / sqrtf(128.0f);
+    a.capacity = capacity;
+    return a;
+}
 
 int Qwen3Engine::forward(int token, int pos, float* logits_out, cudaStream_t s) {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;

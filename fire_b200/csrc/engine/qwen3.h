@@ -27,6 +27,7 @@
 #include "engine/arena.h"
 #include "engine/nccl_shim.h"
 #include "kernels/decode_state.h"
+#include "kernels/layer_stack.h"
 
 namespace fb {
 
@@ -96,11 +97,18 @@ class Qwen3Engine {
     int tp_size() const { return tp_; }
     int tp_rank() const { return rank_; }
 
+    bool uses_layer_stack() const { return stack_; }
+    // Timeline of the last layer-stack launch ([grid][layers][5][5] %globaltimer stamps,
+    // see StackArgs::trace); returns the word count, 0 when tracing is off.
+    int64_t stack_trace(uint64_t* host_out, int64_t capacity_words) const;
+
   private:
     Qwen3Engine() = default;
+    StackArgs stack_template(int capacity) const;
     int import_weights(const std::vector<TensorSrc>& tensors, std::string* err);
     int enqueue_step(cudaStream_t s, bool sample);
     int capture(bool sample, cudaGraphExec_t* exec);
+    int capture_once(bool sample, cudaGraphExec_t* exec);
     int launch_step(cudaStream_t s, bool sample);
 
     Qwen3Dims d_;
@@ -119,6 +127,7 @@ class Qwen3Engine {
         float* k_norm = nullptr;
         float* ffn_norm = nullptr;
         W4Mat qkv, o, gu, down;
+        uint8_t *qkv_items = nullptr, *o_items = nullptr, *gu_items = nullptr, *down_items = nullptr;
     };
     std::vector<Layer> layers_;
     void* embedding_ = nullptr;
@@ -143,6 +152,16 @@ class Qwen3Engine {
     int32_t* host_token_ = nullptr;      // pinned
     cudaGraphExec_t graph_fwd_ = nullptr, graph_step_ = nullptr;
     NcclComm comm_ = nullptr;
+
+    // persistent layer-stack kernel (tensor-parallel size 1): weights in item layout
+    bool stack_ = false;
+    bool stack_coop_ = true;  // cooperative launch (falls back if the runtime refuses it)
+    StackLayer* stack_layers_ = nullptr;  // device [layers]
+    StackArgs stack_args_{};
+    unsigned* stack_sync_ = nullptr;
+    size_t stack_sync_bytes_ = 0;
+    bool stack_trace_on_ = false;  // FIRE_B200_STACK_TRACE=1: record the per-phase timeline
+    size_t stack_trace_words_ = 0;
 };
 
 }  // namespace fb

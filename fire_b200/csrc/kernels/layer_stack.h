@@ -1,0 +1,110 @@
+// Persistent decode kernel for the whole Qwen3 layer stack (one GPU, tensor-parallel
+// size 1): the per-layer sequence of Fire's Qwen3Model::forward
+// (src/model/qwen.cpp:190-292) as one launch.
+//
+// Every INT4 projection is stored as "items" of 16 rows x 256 K (2208 bytes) in the
+// order the kernel reads them. One CTA runs per SM: a producer warp streams every item
+// the CTA will consume in this step (all layers, all phases, plus the attention K/V
+// rows) into a shared-memory ring with TMA bulk copies, while 16 consumer warps run the
+// phases qkv -> attention -> o -> gate/up -> down of each layer. A phase waits on a
+// device-wide counter of the CTAs that finished the phase it depends on; the weight
+// stream does not wait, so HBM stays busy across phase boundaries.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "decode_state.h"
+
+namespace fb {
+
+constexpr int kItemRows = 16;
+constexpr int kItemK = 256;
+// weights 16 rows x 2 groups x 64 bytes (MMA fragment order) | scales f32 [16][2] | zeros u8 [16][2]
+constexpr int kItemBytes = 2208;
+constexpr int kItemScaleOff = 2048;
+constexpr int kItemZeroOff = 2176;
+constexpr int kStackPhases = 5;  // 0 qkv, 1 attention, 2 o, 3 gate/up, 4 down
+constexpr int kStackConsumerWarps = 16;
+constexpr int kStackThreads = (kStackConsumerWarps + 1) * 32;
+constexpr int kStackChunk = 128;  // keys per attention unit
+constexpr int kStackMaxGroup = 8;  // q heads per KV head
+constexpr int kStackErrTimeout = 3;  // DecodeState::error when a bounded wait gave up
+constexpr int kStackTraceSlots = 7;
+
+enum StackPackMode : int { kPackRows = 0, kPackGateUp = 1 };
+
+// Bytes of the item layout of an [N, K] matrix (N % 16 == 0, K % 256 == 0).
+size_t stack_items_bytes(int N, int K);
+// Repack an INT4 group-128 matrix (qweight u8 [N, K/2], scales f32 [N, K/128],
+// zero points u8 [N, K/128]) into items. kPackGateUp: source rows [0, N/2) are gate
+// rows and [N/2, N) the matching up rows; item row tile t then holds gate rows
+// 8t..8t+7 followed by up rows 8t..8t+7.
+cudaError_t stack_pack_launch(const uint8_t* qw, const float* scales, const uint8_t* zeros, int N, int K,
+                              int mode, uint8_t* out, cudaStream_t s);
+
+struct StackLayer {
+    const float* attn_norm;
+    const float* ffn_norm;
+    const float* q_norm;
+    const float* k_norm;
+    const uint8_t* qkv;   // [q | k | v] rows x hidden
+    const uint8_t* o;     // hidden x q_dim
+    const uint8_t* gu;    // kPackGateUp, 2*inter x hidden
+    const uint8_t* down;  // hidden x inter
+};
+
+struct StackPhase {  // GEMV phase geometry, identical in every layer
+    int n, k;
+    int tiles;   // n / 16
+    int ipr;     // items per row tile (k / 256)
+    int kparts;  // K splits (their partial sums are added in a fixed order)
+    int ipu;     // items per unit (ipr / kparts)
+    int units;   // tiles * kparts
+};
+
+struct StackArgs {
+    const StackLayer* layers;  // device array [L]
+    int L;
+    int hidden, q_dim, kv_dim, inter;
+    int q_heads, kv_heads;
+    float eps, scale;
+    DecodeState* state;
+    float* hidden_buf;  // residual stream in / out
+    float* attn_res;    // hidden + o projection
+    float* qkv;
+    float* attn_out;
+    float* act;
+    float* kcache;  // [L][capacity][kv_dim]
+    float* vcache;
+    int capacity;
+    int max_chunks;  // ceil(capacity / kStackChunk)
+    const float* rope_sin;  // [capacity][64]
+    const float* rope_cos;
+    float* attn_part;  // [q_heads][max_chunks][128]
+    float* attn_ml;    // [q_heads][max_chunks][2]
+    float* kpart;      // split-K partial sums [kparts][n]
+    unsigned* sync;    // phase counters, attention and tile tickets: zero before each launch
+    // optional timeline [grid][L][kStackPhases][kStackTraceSlots] of %globaltimer stamps:
+    // 0 phase entered, 1 input dependency met, 2 input staged, 3 the CTA's last unit
+    // done, 4 the producer issued the phase's last item (0 where the CTA had no units);
+    // then SM cycles: 5 consumer warps waiting for ring items (summed over warps),
+    // 6 the producer waiting for free slots
+    unsigned long long* trace;
+    StackPhase ph[kStackPhases];  // index 1 (attention) unused
+    // shared-memory plan (filled by stack_plan)
+    int grid;
+    int ring_slots;
+    int max_units;    // GEMV units one CTA owns in one phase, at most
+    int part_stride;  // floats per unit partial slot (max ipu * 16)
+    int off_bar, off_x, off_part, off_ucnt, off_misc;
+    int smem_bytes;
+};
+
+size_t stack_sync_words(const StackArgs& a);
+size_t stack_kpart_floats(const StackArgs& a);
+// Fill the phase geometry and the shared-memory plan for `grid` CTAs; false when the
+// shapes are outside what the kernel handles (the per-op kernels then run instead).
+bool stack_plan(StackArgs* a, int grid);
+cudaError_t stack_launch(const StackArgs& a, cudaStream_t s, bool cooperative);
+
+}  // namespace fb

@@ -138,6 +138,18 @@ class Qwen3Engine:
     def kernels_per_step(self) -> int:
         return self._L.fire_b200_qwen3_kernels_per_step(self._h)
 
+    def stack_trace(self) -> np.ndarray:
+        """Per-phase timeline of the last layer-stack launch, [CTAs, layers, 5, 7] stamps
+        (empty unless FIRE_B200_STACK_TRACE=1 was set when the engine was created)."""
+        n = int(self._L.fire_b200_qwen3_stack_trace(self._h, None, 0))
+        if n <= 0:
+            return np.zeros((0,), np.uint64)
+        out = np.zeros(n, np.uint64)
+        got = int(self._L.fire_b200_qwen3_stack_trace(self._h, out.ctypes.data, n))
+        if got < 0:
+            raise N.FireB200Error(got, "stack trace read failed")
+        return out.reshape(-1, self.profile.num_layers, 5, 7)
+
     @property
     def step_weight_bytes(self) -> int:
         return int(self._L.fire_b200_qwen3_step_weight_bytes(self._h))

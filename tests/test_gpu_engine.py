@@ -111,6 +111,17 @@ def test_engine_open_fire_file_matches_create(cuda, tmp_path):
     assert torch.equal(la, lb)
 
 
+@pytest.mark.parametrize("profile", [TINY, SMALL])
+def test_engine_uses_layer_stack_kernel(cuda, profile):
+    """At tensor-parallel size 1 a decode step is embedding, the persistent layer-stack
+    kernel, the LM head and argmax (unless FIRE_B200_LAYER_STACK=0)."""
+    if os.environ.get("FIRE_B200_LAYER_STACK") == "0":
+        pytest.skip("per-op path selected")
+    w = synth.generate(profile, "int4", seed=1)
+    eng = Qwen3Engine(profile, w)
+    assert eng.kernels_per_step == 4
+
+
 def test_engine_rejects_bad_arguments_without_advancing(cuda):
     p = TINY
     w = synth.generate(p, "int4", seed=2)
