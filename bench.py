@@ -12,7 +12,10 @@ decode from the end of the prompt, ending at context 2048.
            step is one CUDA graph per token) -> tokens/s
   e2e    = the reference's host loop through the C ABI (per token: H2D of the input id
            from pinned memory, one step, D2H of the sampled id, stream synchronise)
-  roofline = the INT4 GEMV (the dominant kernel), timed live on the decode shapes
+  roofline = the dominant kernel, timed live: at TP1 the persistent layer-stack kernel
+           (all 36 layers in one launch; bytes = INT4 weights + scales/zeros + the FP32
+           K/V rows it reads + norms), under tensor parallelism the INT4 GEMV on the
+           decode shapes
 
 `--impl reference` times the CPU restatement of the same decode (oracle/, FP32 on the
 host cores) on a bounded sample of the workload (see `cpu_baseline.sample`).
@@ -255,6 +258,19 @@ def time_w4_gemv(stream, reps: int = 4):
     return by / launches, ms * 1e3 / launches  # bytes per launch, us per launch
 
 
+def layer_stack_bytes(p, world: int, pos: int) -> float:
+    """Algorithmic HBM bytes of one layer-stack launch at position `pos`: per layer the
+    INT4 q/k/v, o, gate/up and down matrices (0.5 B per weight, 4 B scale + 1 B zero point
+    per 128-group), the RMSNorm weights, the FP32 K and V rows 0..pos-1 and the row it
+    writes at pos."""
+    H, F, Q, KV = p.hidden_size, p.intermediate_size // world, p.q_dim // world, p.kv_dim // world
+    mats = [(Q + 2 * KV, H), (H, Q), (2 * F, H), (H, F)]
+    w = sum(n * k // 2 + n * (k // 128) * 5 for n, k in mats)
+    norms = (2 * H + 2 * 128) * 4
+    kv = 2 * (pos + 1) * KV * 4
+    return float(p.num_layers * (w + norms + kv))
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -336,12 +352,19 @@ def run_ours(args):
     barrier()
     ms_e2e = max(h0.elapsed_time(h1), wall_e2e * 1e3)
     # roofline of the dominant kernel, measured live
-    w4_bytes, w4_us = time_w4_gemv(stream)
+    if eng.kernels_per_step == 4:  # persistent layer-stack kernel
+        pos = eng.length
+        kern_name = "stack_kernel"
+        kern_bytes = layer_stack_bytes(p, world, pos)
+        kern_us = eng.time_layer_stack(5, stream=stream) * 1e3
+    else:
+        kern_name = "w4g128_gemv_kernel"
+        kern_bytes, kern_us = time_w4_gemv(stream)
     # max over ranks
     if world > 1:
-        t = torch.tensor([ms, ms_e2e, w4_us], dtype=torch.float64)
+        t = torch.tensor([ms, ms_e2e, kern_us], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_e2e, w4_us = t.tolist()
+        ms, ms_e2e, kern_us = t.tolist()
     clocks = clk.summary()
     cpu = None
     if cpu_w is not None:
@@ -358,8 +381,8 @@ def run_ours(args):
         per_tok_s = (ms / 1e3) / (n_gen * args.steps)
         traffic = None
         try:
-            traffic = json.load(open(os.path.join(ROOT, "profiles", "w4_gemv_traffic.json"))).get(
-                "bytes_per_launch_scaled")
+            tr = json.load(open(os.path.join(ROOT, "profiles", "dram_traffic.json")))
+            traffic = tr.get(kern_name, {}).get("bytes_per_launch_scaled")
         except (OSError, ValueError):
             pass
         line = {
@@ -373,9 +396,9 @@ def run_ours(args):
             "e2e": {"value": tok_s_e2e, "unit": "tok/s", "h2d_bytes_per_step": 16 * n_gen,
                     "d2h_bytes_per_step": 4 * n_gen},
             "gpu_launches": (eng.kernels_per_step * n_gen + 1) * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "w4g128_gemv_kernel", "achieved": w4_bytes / (w4_us * 1e3),
-                         "peak": peak, "unit": "GB/s", "frac": w4_bytes / (w4_us * 1e3) / peak,
-                         "traffic": traffic, "bytes_per_launch": w4_bytes, "us_per_launch": w4_us,
+            "roofline": {"bound": "hbm", "kernel": kern_name, "achieved": kern_bytes / (kern_us * 1e3),
+                         "peak": peak, "unit": "GB/s", "frac": kern_bytes / (kern_us * 1e3) / peak,
+                         "traffic": traffic, "bytes_per_launch": kern_bytes, "us_per_launch": kern_us,
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "when" in pk else "fallback"},
             "decode_roofline": {"bytes_per_token_per_gpu": step_bytes, "achieved": step_bytes / per_tok_s / 1e9,
                                 "unit": "GB/s", "frac": step_bytes / per_tok_s / 1e9 / peak,

@@ -37,6 +37,7 @@ SIGNATURES: dict = {
     "fire_b200_qwen3_logits": (_vp, [_vp]),
     "fire_b200_qwen3_kernels_per_step": (_i, [_vp]),
     "fire_b200_qwen3_stack_trace": (C.c_int64, [_vp, _vp, C.c_int64]),
+    "fire_b200_qwen3_time_layer_stack": (_i, [_vp, _i, C.POINTER(C.c_float), _vp]),
     "fire_b200_qwen3_step_weight_bytes": (C.c_uint64, [_vp]),
     "fire_b200_qwen3_destroy": (None, [_vp]),
 }

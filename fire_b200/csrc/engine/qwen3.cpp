@@ -654,6 +654,30 @@ int Qwen3Engine::kernels_per_step() const {
     return 5 * d_.layers + 3 + (tp_ > 1 ? 1 : 0);
 }
 
+int Qwen3Engine::time_layer_stack(int reps, float* ms_out, cudaStream_t s) {
+    if (!stack_ || capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (reps <= 0 || ms_out == nullptr || length_ >= capacity_) return FIRE_B200_ERR_INVALID;
+    FB_CK(set_state_launch(state_, 0, length_, 0, s, false));
+    cudaEvent_t e0, e1;
+    FB_CK(cudaEventCreate(&e0));
+    FB_CK(cudaEventCreate(&e1));
+    int rc = 0;
+    for (int i = 0; i <= reps && rc == 0; ++i) {  // launch 0 warms up
+        if (i == 1) rc = static_cast<int>(cudaEventRecord(e0, s));
+        if (!rc) rc = static_cast<int>(cudaMemsetAsync(stack_sync_, 0, stack_sync_bytes_, s));
+        if (!rc) rc = static_cast<int>(stack_launch(stack_args_, s, stack_coop_));
+    }
+    if (!rc) rc = static_cast<int>(cudaEventRecord(e1, s));
+    if (!rc) rc = static_cast<int>(cudaEventSynchronize(e1));
+    float ms = 0.0f;
+    if (!rc) rc = static_cast<int>(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc) return rc;
+    *ms_out = ms / static_cast<float>(reps);
+    return 0;
+}
+
 int64_t Qwen3Engine::stack_trace(uint64_t* host_out, int64_t capacity_words) const {
     if (!stack_args_.trace || !stack_trace_words_) return 0;
     const int64_t n = static_cast<int64_t>(stack_trace_words_);

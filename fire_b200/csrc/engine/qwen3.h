@@ -101,6 +101,9 @@ class Qwen3Engine {
     // Timeline of the last layer-stack launch ([grid][layers][5][5] %globaltimer stamps,
     // see StackArgs::trace); returns the word count, 0 when tracing is off.
     int64_t stack_trace(uint64_t* host_out, int64_t capacity_words) const;
+    // Average device time (ms) of `reps` launches of the layer-stack kernel alone at
+    // position length() (the KV row there is rewritten; the length does not change).
+    int time_layer_stack(int reps, float* ms_out, cudaStream_t s);
 
   private:
     Qwen3Engine() = default;

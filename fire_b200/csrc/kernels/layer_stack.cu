@@ -36,7 +36,10 @@ namespace {
 
 constexpr int W = kStackConsumerWarps;
 constexpr int kConsumers = W * 32;
-constexpr int kSpinLimit = 1 << 22;
+// Every wait gives up after kWaitNs of GPU time (a healthy wait lasts microseconds);
+// kSpinLimit is only a backstop on the number of polls.
+constexpr unsigned long long kWaitNs = 200ull * 1000 * 1000;
+constexpr int kSpinLimit = 1 << 26;
 constexpr int kMaxG = kStackMaxGroup;
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -77,6 +80,10 @@ __device__ __forceinline__ unsigned long long gtime() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// true once `t0` lies more than kWaitNs in the past (checked every 64 polls)
+__device__ __forceinline__ bool overdue(int i, unsigned long long t0) {
+    return (i & 63) == 63 && gtime() - t0 > kWaitNs;
+}
 __device__ __forceinline__ void stamp(const StackArgs& a, int l, int p, int k) {
     if (a.trace != nullptr)
         a.trace[((static_cast<size_t>(blockIdx.x) * a.L + l) * kStackPhases + p) * kStackTraceSlots + k] = gtime();
@@ -107,7 +114,7 @@ struct Shared {
     uint64_t* full;
     uint64_t* empty;
     uint8_t* x;       // digits [groups][4 digits][4 quads][4 mma][8 B], then float2 [groups]
-    float* part;      // [max_units][part_stride]
+    float* part;      // [units of the phase][ipu][16] per-item row sums
     int* ucnt;        // [max_units]
     float* red;       // [32]
     int* misc;        // [0] failed flag, [2] attention "last" flag, [4..5] traced wait cycles (u64)
@@ -200,12 +207,14 @@ __device__ void producer(const StackArgs& a, const Shared& sh, const Sched& sc, 
         if (seq < static_cast<unsigned>(S)) return true;
         uint64_t* b = &sh.empty[slot];
         const long long c0 = a.trace != nullptr ? clock64() : 0;
+        const unsigned long long t0 = gtime();
         for (int i = 0; i < kSpinLimit; ++i) {
             if (mbar_try(b, parity ^ 1u)) {
                 if (a.trace != nullptr) waited += clock64() - c0;
                 return true;
             }
             if ((i & 255) == 255 && state_failed(a.state)) return false;
+            if (overdue(i, t0)) break;
         }
         record_timeout(a.state);
         return false;
@@ -217,6 +226,7 @@ __device__ void producer(const StackArgs& a, const Shared& sh, const Sched& sc, 
             cur.slot -= S;
             cur.parity ^= 1u;
         }
+        if (lane == 0) *reinterpret_cast<volatile unsigned*>(&sh.misc[6]) = cur.seq;  // for the L2 prefetcher
     };
     const size_t kv_stride = static_cast<size_t>(a.kv_dim);
     for (int l = 0; l < a.L && ok; ++l) {
@@ -254,26 +264,30 @@ __device__ void producer(const StackArgs& a, const Shared& sh, const Sched& sc, 
                     }
                 }
             } else {
-                const StackPhase& ph = a.ph[p];  // ipu <= 16
+                const StackPhase& ph = a.ph[p];
                 const uint8_t* items = phase_items(Ly, p);
                 for (int k = 0; k < count && ok; ++k) {
                     const int u = first + k * sc.grid;
                     const int tile = u / ph.kparts, kp = u % ph.kparts;
-                    bool mine_ok = true;
-                    if (lane < ph.ipu) {
-                        int slot;
-                        unsigned parity;
-                        lane_slot(&slot, &parity);
-                        mine_ok = acquire(cur.seq + lane, slot, parity);
-                        if (mine_ok) {
-                            const uint8_t* src = items + (static_cast<size_t>(tile) * ph.ipr +
-                                                          static_cast<size_t>(kp) * ph.ipu + lane) * kItemBytes;
-                            mbar_expect_tx(&sh.full[slot], kItemBytes);
-                            bulk_load(sh.ring + static_cast<size_t>(slot) * kItemBytes, src, kItemBytes, &sh.full[slot]);
+                    const uint8_t* unit = items + (static_cast<size_t>(tile) * ph.ipr + static_cast<size_t>(kp) * ph.ipu) * kItemBytes;
+                    // the unit's items in steps of at most 32 (one per lane)
+                    for (int j0 = 0; j0 < ph.ipu && ok; j0 += 32) {
+                        const int m = min(32, ph.ipu - j0);
+                        bool mine_ok = true;
+                        if (lane < m) {
+                            int slot;
+                            unsigned parity;
+                            lane_slot(&slot, &parity);
+                            mine_ok = acquire(cur.seq + lane, slot, parity);
+                            if (mine_ok) {
+                                mbar_expect_tx(&sh.full[slot], kItemBytes);
+                                bulk_load(sh.ring + static_cast<size_t>(slot) * kItemBytes,
+                                          unit + static_cast<size_t>(j0 + lane) * kItemBytes, kItemBytes, &sh.full[slot]);
+                            }
                         }
+                        ok = !__any_sync(0xffffffffu, !mine_ok);
+                        advance(m);
                     }
-                    ok = !__any_sync(0xffffffffu, !mine_ok);
-                    advance(ph.ipu);
                 }
             }
             if (count > 0 && lane == 0) {
@@ -294,8 +308,69 @@ __device__ void producer(const StackArgs& a, const Shared& sh, const Sched& sc, 
                 slot = S - 1;
                 parity ^= 1u;
             }
+            const unsigned long long t0 = gtime();
             for (int it = 0; it < kSpinLimit; ++it)
-                if (mbar_try(&sh.full[slot], parity)) break;
+                if (mbar_try(&sh.full[slot], parity) || overdue(it, t0)) break;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// L2 prefetcher: walks the producer's item sequence kStackPrefetchAhead items ahead of
+// the ring and asks L2 to fetch each item (weights: one 2208-byte item per lane; K/V:
+// one 512-byte row per lane), so phases that stall on latency keep HBM busy and the ring
+// refills from L2. Prefetches carry no completion, so this warp never blocks the others.
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ void prefetcher(const StackArgs& a, const Shared& sh, const Sched& sc, int pos) {
+    const int lane = threadIdx.x & 31;
+    unsigned seq = 0;
+    // wait (bounded) until the ring producer is within reach of item `upto`
+    auto throttle = [&](unsigned upto) -> bool {
+        const unsigned long long t0 = gtime();
+        for (int i = 0; i < kSpinLimit; ++i) {
+            const unsigned prod = *reinterpret_cast<volatile unsigned*>(&sh.misc[6]);
+            if (prod + kStackPrefetchAhead >= upto) return true;
+            if (*reinterpret_cast<volatile int*>(&sh.misc[0]) != 0 || overdue(i, t0)) return false;
+            __nanosleep(200);
+        }
+        return false;
+    };
+    const size_t kv_stride = static_cast<size_t>(a.kv_dim);
+    for (int l = 0; l < a.L; ++l) {
+        const StackLayer& Ly = a.layers[l];
+        for (int p = 0; p < kStackPhases; ++p) {
+            int first, count;
+            sc.mine(a, l, p, &first, &count);
+            if (p == 1) {
+                const size_t layer_off = static_cast<size_t>(l) * a.capacity * kv_stride;
+                for (int k = 0; k < count; ++k) {
+                    const int u = first + k * sc.grid;
+                    const int c = u / a.kv_heads, h = u % a.kv_heads;
+                    const int t0 = c * kStackChunk, ni = sc.att_items(c);
+                    const int rows = min(kStackChunk, pos - t0);  // rows t < pos
+                    for (int half = 0; half < 2; ++half) {
+                        if (!throttle(seq + ni)) return;
+                        const float* base = (half ? a.vcache : a.kcache) + layer_off + static_cast<size_t>(h) * 128;
+                        for (int r = lane; r < rows; r += 32) prefetch_l2(base + static_cast<size_t>(t0 + r) * kv_stride, 512u);
+                        seq += ni;
+                    }
+                }
+            } else {
+                const StackPhase& ph = a.ph[p];
+                const uint8_t* items = phase_items(Ly, p);
+                for (int k = 0; k < count; ++k) {
+                    if (!throttle(seq + ph.ipu)) return;
+                    const int u = first + k * sc.grid;
+                    const int tile = u / ph.kparts, kp = u % ph.kparts;
+                    const uint8_t* unit =
+                        items + (static_cast<size_t>(tile) * ph.ipr + static_cast<size_t>(kp) * ph.ipu) * kItemBytes;
+                    for (int j = lane; j < ph.ipu; j += 32) prefetch_l2(unit + static_cast<size_t>(j) * kItemBytes, kItemBytes);
+                    seq += ph.ipu;
+                }
+            }
         }
     }
 }
@@ -319,12 +394,13 @@ __device__ __forceinline__ Slot slot_of(unsigned seq, int S) {
     return Slot{static_cast<int>(seq - q * static_cast<unsigned>(S)), q & 1u};
 }
 
-__device__ bool wait_item(const StackArgs& a, const Shared& sh, Slot sl) {
+__device__ bool wait_item(const StackArgs& a, const Shared& sh, Slot sl, long long& waited) {
     const unsigned parity = sl.parity;
     uint64_t* b = &sh.full[sl.index];
-    if (a.trace == nullptr && __all_sync(0xffffffffu, mbar_try(b, parity))) return true;  // common case
+    if (__all_sync(0xffffffffu, mbar_try(b, parity))) return true;  // common case: already landed
     if (__any_sync(0xffffffffu, failed(sh))) return false;
     const long long c0 = a.trace != nullptr ? clock64() : 0;
+    const unsigned long long t0 = gtime();
     bool ok = false;
     for (int i = 0; i < kSpinLimit; ++i) {
         if (mbar_try(b, parity)) {
@@ -332,9 +408,9 @@ __device__ bool wait_item(const StackArgs& a, const Shared& sh, Slot sl) {
             break;
         }
         if ((i & 255) == 255 && state_failed(a.state)) break;
+        if (overdue(i, t0)) break;
     }
-    if (a.trace != nullptr && (threadIdx.x & 31) == 0)
-        atomicAdd(reinterpret_cast<unsigned long long*>(sh.misc + 4), static_cast<unsigned long long>(clock64() - c0));
+    if (a.trace != nullptr) waited += clock64() - c0;
     if (__all_sync(0xffffffffu, ok)) return true;
     if ((threadIdx.x & 31) == 0) {
         if (!state_failed(a.state)) record_timeout(a.state);
@@ -352,9 +428,11 @@ __device__ void wait_phase(const StackArgs& a, const Shared& sh, int l, int p, u
     if (threadIdx.x == 0 && !failed(sh)) {
         const unsigned* ctr = a.sync + l * kStackPhases + p;
         bool ok = false;
+        const unsigned long long t0 = gtime();
         for (int i = 0; i < kSpinLimit; ++i) {
             if (ld_acquire(ctr) >= target) { ok = true; break; }
             if ((i & 63) == 63 && state_failed(a.state)) break;
+            if (overdue(i, t0)) break;
             __nanosleep(32);
         }
         if (!ok) {
@@ -382,9 +460,8 @@ __device__ float csum(float v, float* red) {
 // digits hold x * w; the scalar 1/rms multiplies the row sums in the epilogue (the same
 // product, reassociated), so no block-wide reduction sits between the input and the
 // first MMA: each warp leaves its sum of squares in red[warp].
-// `own`: a unit has exactly W items and warps w, w + 8 consume items 2(w%8) and
-// 2(w%8)+1 of their units, so the pair stages just those groups (2 per K part each) and
-// syncs on a 64-thread named barrier instead of a consumer-wide one.
+// `own`: a unit has exactly W items and warp w consumes item w of every unit, so it
+// stages only the groups of those items (2 per K part) and needs no barrier after.
 // Otherwise warp w stages groups w, w + W, ... and the consumers sync afterwards.
 constexpr int kStageRegs = 8;
 
@@ -392,37 +469,35 @@ __device__ __forceinline__ void store_digits(const float (&v)[4], int g, const S
     const int lane = threadIdx.x & 31;
     uint8_t* xd = sh.x;
     float2* xg = reinterpret_cast<float2*>(sh.x + static_cast<size_t>(groups) * 512);
-    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    m = warp_max(m);
-    // m in [2^ex, 2^(ex+1)): x * 2^(25-ex) has magnitude < 2^26
-    const int ex = static_cast<int>((__float_as_uint(m) >> 23) & 0xFF) - 127;
+    // group max of |v| (non-negative floats order like their bit patterns)
+    const uint32_t mb = max(max(__float_as_uint(fabsf(v[0])), __float_as_uint(fabsf(v[1]))),
+                            max(__float_as_uint(fabsf(v[2])), __float_as_uint(fabsf(v[3]))));
+    const uint32_t gm = __reduce_max_sync(0xffffffffu, mb);
+    // max in [2^ex, 2^(ex+1)): x * 2^(25-ex) has magnitude < 2^26
+    const int ex = static_cast<int>((gm >> 23) & 0xFF) - 127;
     int sh_ = 25 - ex;
-    if (m == 0.0f || sh_ > 126) sh_ = 126;
+    if (gm == 0 || sh_ > 126) sh_ = 126;
     const float up = __uint_as_float(static_cast<uint32_t>(127 + sh_) << 23);
     const float down = __uint_as_float(static_cast<uint32_t>(127 - sh_) << 23);
     int fx[4];
-    long long sum = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        fx[e] = __float2int_rn(v[e] * up);
-        sum += fx[e];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) xg[g] = make_float2(static_cast<float>(sum), down);
+    for (int e = 0; e < 4; ++e) fx[e] = __float2int_rn(v[e] * up);
+    // exact integer group sum: |lane sum| < 2^28, reduced as 15 high + 13 low bits
+    const int ls = (fx[0] + fx[1]) + (fx[2] + fx[3]);
+    const int shi = __reduce_add_sync(0xffffffffu, ls >> 13);
+    const int slo = __reduce_add_sync(0xffffffffu, ls & 0x1FFF);
+    if (lane == 0) xg[g] = make_float2(fmaf(static_cast<float>(shi), 8192.0f, static_cast<float>(slo)), down);
+    // digits = bit fields of the two's complement: bits 0-6, 7-13, 14-20 (unsigned,
+    // 0..127) and the arithmetic shift by 21 (signed, -32..31); x = d0 + 2^7 d1 + 2^14 d2 + 2^21 d3
     const int c = lane >> 3, j = (lane >> 1) & 3, hi = lane & 1;
-    int r[4] = {fx[0], fx[1], fx[2], fx[3]};
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
         int d[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            d[e] = ((r[e] + 64) & 127) - 64;
-            r[e] = (r[e] - d[e]) >> 7;
-        }
+        for (int e = 0; e < 4; ++e) d[e] = n < 3 ? (fx[e] >> (7 * n)) & 127 : fx[e] >> 21;
         uint8_t* slot = xd + (((static_cast<size_t>(g) * 4 + n) * 4 + c) * 4 + j) * 8;
-        *reinterpret_cast<uint16_t*>(slot + 2 * hi) = static_cast<uint16_t>((d[0] & 0xFF) | ((d[2] & 0xFF) << 8));
-        *reinterpret_cast<uint16_t*>(slot + 4 + 2 * hi) = static_cast<uint16_t>((d[1] & 0xFF) | ((d[3] & 0xFF) << 8));
+        *reinterpret_cast<uint16_t*>(slot + 2 * hi) = static_cast<uint16_t>(__byte_perm(d[0], d[2], 0x0040));
+        *reinterpret_cast<uint16_t*>(slot + 4 + 2 * hi) = static_cast<uint16_t>(__byte_perm(d[1], d[3], 0x0040));
     }
 }
 
@@ -432,11 +507,8 @@ __device__ void stage_x(const float* x, const float* norm_w, const StackPhase& p
     const int mine = own ? 2 * ph.kparts : (groups - warp + W - 1) / W;  // groups this warp stages
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const float4* w4 = reinterpret_cast<const float4*>(norm_w);
-    // own: warps w and w + 8 consume items 2(w%8), 2(w%8)+1 of every K part (groups
-    // 4(w%8)..4(w%8)+3); warp w < 8 stages the first two, warp w + 8 the last two
-    auto group_of = [&](int i) {
-        return own ? 2 * W * (i >> 1) + 4 * (warp & 7) + 2 * (warp >> 3) + (i & 1) : warp + i * W;
-    };
+    // own: warp w consumes item w of every unit, i.e. groups 2(kp*W + w) + {0, 1}
+    auto group_of = [&](int i) { return own ? 2 * ((i >> 1) * W + warp) + (i & 1) : warp + i * W; };
     float ss = 0.0f;
     for (int b0 = 0; b0 < mine; b0 += kStageRegs) {
         float4 v[kStageRegs];
@@ -519,7 +591,7 @@ __device__ __forceinline__ void item_accumulate(const ItemRegs& it, const Shared
         mma_u8s8(db, wg[1] & m, wh[1] & m, (wg[1] >> 4) & m, (wh[1] >> 4) & m, b4[0].z, b4[0].w);
         mma_u8s8(da, wg[2] & m, wh[2] & m, (wg[2] >> 4) & m, (wh[2] >> 4) & m, b4[1].x, b4[1].y);
         mma_u8s8(db, wg[3] & m, wh[3] & m, (wg[3] >> 4) & m, (wh[3] >> 4) & m, b4[1].z, b4[1].w);
-        // d_even + 128 d_odd is exact in int32 and in float (|d| <= 128 * 15 * 64)
+        // d_even + 128 d_odd: exact in int32 (|column sum| <= 128 * 15 * 127), one rounding to float
         const int t0 = (da[0] + db[0]) + 128 * (da[1] + db[1]);
         const int t1 = (da[2] + db[2]) + 128 * (da[3] + db[3]);
         const float2 gx = xg[g];
@@ -534,7 +606,13 @@ __device__ __forceinline__ void item_accumulate(const ItemRegs& it, const Shared
 }
 
 // Epilogue of one finished row tile; lane r < 16 holds the full sum of row tile*16 + r.
-__device__ __forceinline__ void tile_epilogue(const StackArgs& a, int p, int tile, float v) {
+// The residual input of a phase's rows (hidden for o, attn_res for down); it is final
+// before the phase starts, so it is read ahead of the epilogue.
+__device__ __forceinline__ const float* phase_residual(const StackArgs& a, int p) {
+    return p == 2 ? a.hidden_buf : (p == 4 ? a.attn_res : nullptr);
+}
+
+__device__ __forceinline__ void tile_epilogue(const StackArgs& a, int p, int tile, float v, float res) {
     const int lane = threadIdx.x & 31;
     const float up = __shfl_down_sync(0xffffffffu, v, 8);
     if (lane >= 16) return;
@@ -542,33 +620,33 @@ __device__ __forceinline__ void tile_epilogue(const StackArgs& a, int p, int til
     if (p == 0) {
         a.qkv[row] = v;
     } else if (p == 2) {
-        a.attn_res[row] = __ldcg(a.hidden_buf + row) + v;  // residual (qwen.cpp:262)
+        a.attn_res[row] = res + v;  // residual (qwen.cpp:262)
     } else if (p == 3) {
         if (lane < 8) {
             const float silu = v * 1.0f / (1.0f + expf(-v));  // swiglu_kernel.cu:11-12
             a.act[tile * 8 + lane] = silu * up;
         }
     } else {
-        a.hidden_buf[row] = __ldcg(a.attn_res + row) + v;  // residual (qwen.cpp:291)
+        a.hidden_buf[row] = res + v;  // residual (qwen.cpp:291)
     }
 }
 
 // Finish unit k of this CTA's units in phase p (one warp): add its item partial sums in
 // item order and apply the epilogue; split-K partials meet through a per-tile ticket.
 __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& sc, int p, int first, int k,
-                            float scale) {
+                            float scale, float res) {
     const int lane = threadIdx.x & 31;
     const StackPhase& ph = a.ph[p];
     const int u = first + k * sc.grid;
     const int tile = u / ph.kparts, kp = u % ph.kparts;
     float v = 0.0f;
     if (lane < 16) {
-        const float* pp = sh.part + static_cast<size_t>(k) * a.part_stride + lane;
-        for (int m = 0; m < (ph.ipu + 1) >> 1; ++m) v += pp[m * 16];
+        const float* pp = sh.part + static_cast<size_t>(k) * ph.ipu * 16 + lane;
+        for (int j = 0; j < ph.ipu; ++j) v += pp[j * 16];
         v *= scale;
     }
     if (ph.kparts == 1) {
-        tile_epilogue(a, p, tile, v);
+        tile_epilogue(a, p, tile, v, res);
     } else {
         if (lane < 16) a.kpart[static_cast<size_t>(kp) * ph.n + tile * 16 + lane] = v;
         __threadfence();
@@ -582,7 +660,7 @@ __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& s
             v = 0.0f;
             if (lane < 16)
                 for (int q = 0; q < ph.kparts; ++q) v += __ldcg(a.kpart + static_cast<size_t>(q) * ph.n + tile * 16 + lane);
-            tile_epilogue(a, p, tile, v);
+            tile_epilogue(a, p, tile, v, res);
             if (lane == 0) *ticket = 0u;
         }
     }
@@ -593,40 +671,34 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const StackPhase& ph = a.ph[p];
     const int groups = ph.k >> 7;
-    const int hp = (ph.ipu + 1) >> 1;  // item pairs per unit: a warp takes two neighbouring items
-    const int total = count * hp;
-    for (int P = warp; P < total; P += W) {
-        const int k = P / hp, m = P % hp;
-        const int j0 = 2 * m;
-        const bool two = j0 + 1 < ph.ipu;
-        const Slot s0 = slot_of(seq_base + static_cast<unsigned>(k * ph.ipu + j0), a.ring_slots);
-        Slot s1 = s0;
-        if (++s1.index == a.ring_slots) {
-            s1.index = 0;
-            s1.parity ^= 1u;
-        }
-        if (!wait_item(a, sh, s0)) continue;
-        if (two && !wait_item(a, sh, s1)) continue;
-        const ItemRegs i0 = load_item(sh.ring + static_cast<size_t>(s0.index) * kItemBytes);
-        ItemRegs i1;
-        if (two) i1 = load_item(sh.ring + static_cast<size_t>(s1.index) * kItemBytes);
-        release_item(sh, s0);
-        if (two) release_item(sh, s1);
+    const int total = count * ph.ipu;
+    long long waited = 0;
+    // residual rows of the unit this warp finishes first (k = warp), read ahead
+    const float* resid = phase_residual(a, p);
+    float res0 = 0.0f;
+    if (resid != nullptr && warp < count && lane < 16)
+        res0 = __ldcg(resid + ((first + warp * sc.grid) / ph.kparts) * 16 + lane);
+    for (int s = warp; s < total; s += W) {
+        const int k = s / ph.ipu, j = s % ph.ipu;
+        const Slot sl = slot_of(seq_base + static_cast<unsigned>(s), a.ring_slots);
+        if (!wait_item(a, sh, sl, waited)) continue;
+        const ItemRegs it = load_item(sh.ring + static_cast<size_t>(sl.index) * kItemBytes);
+        release_item(sh, sl);
         const int kp = (first + k * sc.grid) % ph.kparts;
-        const int g0 = 2 * (kp * ph.ipu + j0);
         float acc0 = 0.0f, acc1 = 0.0f;
-        item_accumulate(i0, sh, groups, g0, acc0, acc1);
-        if (two) item_accumulate(i1, sh, groups, g0 + 2, acc0, acc1);
+        item_accumulate(it, sh, groups, 2 * (kp * ph.ipu + j), acc0, acc1);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
         if ((lane & 3) == 0) {
-            float* dst = sh.part + static_cast<size_t>(k) * a.part_stride + m * 16;
+            float* dst = sh.part + static_cast<size_t>(k) * ph.ipu * 16 + j * 16;
             dst[lane >> 2] = acc0;
             dst[(lane >> 2) + 8] = acc1;
         }
     }
+    if (a.trace != nullptr && lane == 0 && waited > 0)
+        atomicAdd(reinterpret_cast<unsigned long long*>(sh.misc + 4), static_cast<unsigned long long>(waited));
     // all items of the phase are in: finish the units in parallel, then one thread
     // publishes the phase (barrier, then fence + counter: every epilogue store of this
     // CTA is ordered before the counter update)
@@ -639,7 +711,12 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
             for (int w = 0; w < W; ++w) ss += sh.red[w];
             scale = 1.0f / sqrtf(ss / static_cast<float>(ph.k) + a.eps);
         }
-        for (int k = warp; k < count; k += W) finish_unit(a, sh, sc, p, first, k, scale);
+        for (int k = warp; k < count; k += W) {
+            float res = res0;
+            if (k != warp && resid != nullptr && lane < 16)
+                res = __ldcg(resid + ((first + k * sc.grid) / ph.kparts) * 16 + lane);
+            finish_unit(a, sh, sc, p, first, k, scale, res);
+        }
     }
     cbar();
     if (threadIdx.x == 0 && !failed(sh)) {
@@ -651,12 +728,14 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
     }
 }
 
-// One attention unit (MG >= q heads per KV head): KV head h, keys [128c, 128c + T); all consumer warps.
-template <int MG>
+// One attention unit (G q heads per KV head): KV head h, keys [128c, 128c + T); all consumer warps.
+template <int G>
 __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched& sc, int l, int pos, int c, int h,
-                               unsigned base) {
+                               unsigned base, bool traced) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = a.q_heads / a.kv_heads;
+    auto mark = [&](int k) {
+        if (traced && tid == 0) stamp(a, l, 1, k);
+    };
     const int t0 = c * kStackChunk;
     const int T = min(kStackChunk, sc.n - t0);
     const int ni = (T + 3) >> 2;
@@ -665,7 +744,8 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
     float* kp = qs + G * 128;                     // [128] this position's rotated k
     float* vp = kp + 128;                         // [128] and v
     float* wml = vp + 128;                        // [W][G][2] per-warp softmax max / sum
-    float* ml = wml + 2 * W * kMaxG;              // [G][2] merge scratch
+    float* wf = wml + 2 * W * kMaxG;              // [W][G] merge factors exp(m_w - M)
+    float* ml = wf + W * kMaxG;                   // [G][2] merge scratch
     float* vpart = ml + 2 * kMaxG;                // [W][G][128]
     float* wc = vpart + W * G * 128;              // [G][max_chunks]
     const bool dead = failed(sh);
@@ -692,24 +772,27 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
         reinterpret_cast<float4*>(a.vcache + row)[lane] = v4;
     }
     cbar();
+    mark(2);
     // Each warp takes items i = warp, warp + W (ni <= 32, so at most two): scores of its
     // keys, a local softmax (max m, sum l) and the unnormalised P.V over its keys, all
     // in registers; the warps' (m, l, o) are merged below (flash-decoding merge).
     // Scores: lanes 8*kk..8*kk+7 hold key kk of an item, float4 sub + 8m of its row.
     const int kk = lane >> 3, sub = lane & 7;
     const int n_keys = sc.n;
-    float scv[2][MG];
+    long long waited = 0;
+    float scv[2][G];
 #pragma unroll
     for (int it = 0; it < 2; ++it)
 #pragma unroll
-        for (int g = 0; g < MG; ++g) scv[it][g] = -INFINITY;
+        for (int g = 0; g < G; ++g) scv[it][g] = -INFINITY;
     bool have[2] = {false, false};
+    const float4* q4 = reinterpret_cast<const float4*>(qs);
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
         const int i = warp + it * W;
         if (i >= ni) break;
         const Slot sl = slot_of(base + static_cast<unsigned>(i), a.ring_slots);
-        if (!wait_item(a, sh, sl)) break;
+        if (!wait_item(a, sh, sl, waited)) break;
         have[it] = true;
         const int t = t0 + 4 * i + kk;
         const float4* src = t == pos ? reinterpret_cast<const float4*>(kp)
@@ -718,50 +801,62 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
 #pragma unroll
         for (int m = 0; m < 4; ++m) kf[m] = t < n_keys ? src[sub + 8 * m] : make_float4(0.f, 0.f, 0.f, 0.f);
         release_item(sh, sl);
+        // all heads advance together (independent chains)
+        float dot[G];
 #pragma unroll
-        for (int g = 0; g < MG; ++g) {
-            if (g >= G) break;
-            const float4* q4 = reinterpret_cast<const float4*>(qs + g * 128);
-            float dot = 0.0f;
+        for (int g = 0; g < G; ++g) dot[g] = 0.0f;
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                const float4 q = q4[sub + 8 * m];
-                dot = fmaf(q.x, kf[m].x, dot);
-                dot = fmaf(q.y, kf[m].y, dot);
-                dot = fmaf(q.z, kf[m].z, dot);
-                dot = fmaf(q.w, kf[m].w, dot);
+        for (int m = 0; m < 4; ++m) {
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float4 q = q4[g * 32 + sub + 8 * m];
+                dot[g] = fmaf(q.x, kf[m].x, dot[g]);
+                dot[g] = fmaf(q.y, kf[m].y, dot[g]);
+                dot[g] = fmaf(q.z, kf[m].z, dot[g]);
+                dot[g] = fmaf(q.w, kf[m].w, dot[g]);
             }
-            dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-            dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-            dot += __shfl_xor_sync(0xffffffffu, dot, 4);
-            scv[it][g] = t < n_keys ? dot * a.scale : -INFINITY;
         }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g) dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], o);
+#pragma unroll
+        for (int g = 0; g < G; ++g) scv[it][g] = t < n_keys ? dot[g] * a.scale : -INFINITY;
     }
+    mark(10);
     // local softmax over this warp's keys (each key is replicated on its 8 lanes)
-    float wm[MG], wl[MG];
-    float4 acc[MG];
+    float wm[G], wl[G];
 #pragma unroll
-    for (int g = 0; g < MG; ++g) {
-        wm[g] = warp_max(fmaxf(scv[0][g], scv[1][g]));
+    for (int g = 0; g < G; ++g) wm[g] = fmaxf(scv[0][g], scv[1][g]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int g = 0; g < G; ++g) wm[g] = fmaxf(wm[g], __shfl_xor_sync(0xffffffffu, wm[g], o));
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
         wl[g] = 0.0f;
-        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (have[0]) {
 #pragma unroll
-            for (int it = 0; it < 2; ++it) {
-                const float e = have[it] ? expf(scv[it][g] - wm[g]) : 0.0f;
-                scv[it][g] = e;
-                wl[g] += sub == 0 ? e : 0.0f;
-            }
-            wl[g] = warp_sum(wl[g]);
+        for (int it = 0; it < 2; ++it) {
+            const float e = have[it] ? expf(scv[it][g] - wm[g]) : 0.0f;
+            scv[it][g] = e;
+            wl[g] += sub == 0 ? e : 0.0f;
         }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int g = 0; g < G; ++g) wl[g] += __shfl_xor_sync(0xffffffffu, wl[g], o);
+    mark(11);
     // unnormalised P.V: lane owns dims 4*lane..4*lane+3 of every head
+    float4 acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
         if (!have[it]) break;
         const int i = warp + it * W;
         const Slot sl = slot_of(base + static_cast<unsigned>(ni + i), a.ring_slots);
-        if (!wait_item(a, sh, sl)) break;
+        if (!wait_item(a, sh, sl, waited)) break;
         const float4* rows = reinterpret_cast<const float4*>(sh.ring + static_cast<size_t>(sl.index) * kItemBytes);
         float4 vv[4];
 #pragma unroll
@@ -773,58 +868,77 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
         release_item(sh, sl);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
+            float pr[G];
 #pragma unroll
-            for (int g = 0; g < MG; ++g) {
-                if (g >= G) break;
-                const float pr = __shfl_sync(0xffffffffu, scv[it][g], q * 8);
-                acc[g].x = fmaf(pr, vv[q].x, acc[g].x);
-                acc[g].y = fmaf(pr, vv[q].y, acc[g].y);
-                acc[g].z = fmaf(pr, vv[q].z, acc[g].z);
-                acc[g].w = fmaf(pr, vv[q].w, acc[g].w);
+            for (int g = 0; g < G; ++g) pr[g] = __shfl_sync(0xffffffffu, scv[it][g], q * 8);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                acc[g].x = fmaf(pr[g], vv[q].x, acc[g].x);
+                acc[g].y = fmaf(pr[g], vv[q].y, acc[g].y);
+                acc[g].z = fmaf(pr[g], vv[q].z, acc[g].z);
+                acc[g].w = fmaf(pr[g], vv[q].w, acc[g].w);
             }
         }
     }
 #pragma unroll
-    for (int g = 0; g < MG; ++g) {
-        if (g >= G) break;
+    for (int g = 0; g < G; ++g) {
         reinterpret_cast<float4*>(vpart + (warp * G + g) * 128)[lane] = acc[g];
         if (lane == 0) {
             wml[(warp * G + g) * 2] = wm[g];
             wml[(warp * G + g) * 2 + 1] = wl[g];
         }
     }
+    if (a.trace != nullptr && lane == 0 && waited > 0)
+        atomicAdd(reinterpret_cast<unsigned long long*>(sh.misc + 4), static_cast<unsigned long long>(waited));
+    mark(12);
     cbar();
-    // this chunk's partial output: merge the warps' (m, l, o) in warp order
+    // this chunk's partial output: merge the warps' (m, l, o) in warp order. Thread
+    // (w, g) turns warp w's max into its factor exp(m_w - M_g).
     const int hq0 = h * G;
+    if (!failed(sh) && tid < W * G) {
+        const int w = tid / G, g = tid % G;
+        float M = -INFINITY;
+#pragma unroll 4
+        for (int v = 0; v < W; ++v) M = fmaxf(M, wml[(v * G + g) * 2]);
+        const float mw = wml[(w * G + g) * 2];
+        wf[w * G + g] = mw == -INFINITY ? 0.0f : expf(mw - M);
+        if (w == 0) ml[2 * g] = M;
+    }
+    cbar();
     if (!failed(sh)) {
         for (int j = tid; j < G * 128; j += kConsumers) {
             const int g = j >> 7, d = j & 127;
-            float M = -INFINITY;
-            for (int w = 0; w < W; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
-            float o = 0.0f, Lsum = 0.0f;
-            for (int w = 0; w < W; ++w) {
-                const float mw = wml[(w * G + g) * 2];
-                if (mw == -INFINITY) continue;
-                const float f = expf(mw - M);
-                o = fmaf(vpart[(w * G + g) * 128 + d], f, o);
-                Lsum = fmaf(wml[(w * G + g) * 2 + 1], f, Lsum);
-            }
+            float o = 0.0f;
+#pragma unroll 4
+            for (int w = 0; w < W; ++w) o = fmaf(vpart[(w * G + g) * 128 + d], wf[w * G + g], o);
             a.attn_part[(static_cast<size_t>(hq0 + g) * a.max_chunks + c) * 128 + d] = o;
             if (d == 0) {
+                float Lsum = 0.0f;
+                for (int w = 0; w < W; ++w) Lsum = fmaf(wml[(w * G + g) * 2 + 1], wf[w * G + g], Lsum);
                 float* dst = a.attn_ml + (static_cast<size_t>(hq0 + g) * a.max_chunks + c) * 2;
-                dst[0] = M;
+                dst[0] = ml[2 * g];
                 dst[1] = Lsum;
             }
         }
     }
-    __threadfence();
+    // publish the chunk: barrier, then one fence + ticket (the consumers' stores above
+    // are ordered before it); the last chunk of the head fences again before reading
     cbar();
+    mark(7);
     unsigned* ticket = a.sync + a.L * kStackPhases + h;
-    if (tid == 0) sh.misc[2] = failed(sh) ? 0 : (atomicAdd(ticket, 1u) == static_cast<unsigned>(sc.nch - 1));
+    if (tid == 0) {
+        int last = 0;
+        if (!failed(sh)) {
+            __threadfence();
+            last = atomicAdd(ticket, 1u) == static_cast<unsigned>(sc.nch - 1);
+            if (last) __threadfence();
+        }
+        sh.misc[2] = last;
+    }
     cbar();
+    mark(8);
     if (sh.misc[2]) {
         // the last chunk of this head combines all chunks (flash-decoding merge)
-        __threadfence();
         for (int g = warp; g < G; g += W) {
             const float* pm = a.attn_ml + static_cast<size_t>(hq0 + g) * a.max_chunks * 2;
             float M = -INFINITY;
@@ -848,12 +962,12 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
             a.attn_out[static_cast<size_t>(hq0 + g) * 128 + d] = o / ml[2 * g + 1];
         }
         if (tid == 0) *ticket = 0u;
-        __threadfence();
     }
     cbar();
+    mark(9);
 }
 
-template <int MG>
+template <int G>
 __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos) {
     const int tid = threadIdx.x;
     unsigned seq = 0;
@@ -876,7 +990,7 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
                 for (int k = 0; k < count; ++k) {
                     const int u = first + k * sc.grid;
                     const int c = u / a.kv_heads, h = u % a.kv_heads;
-                    attention_unit<MG>(a, sh, sc, l, pos, c, h, seq);
+                    attention_unit<G>(a, sh, sc, l, pos, c, h, seq, k == 0);
                     seq += static_cast<unsigned>(2 * sc.att_items(c));
                 }
                 if (tid == 0 && !failed(sh)) {
@@ -896,7 +1010,7 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
                 stage_x(x, nw, ph, own, sh);
             }
             if (own)
-                asm volatile("bar.sync %0, 64;" ::"r"(2 + ((tid >> 5) & 7)) : "memory");
+                __syncwarp();
             else
                 cbar();
             if (tid == 0) stamp(a, l, p, 2);
@@ -906,7 +1020,7 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
     }
 }
 
-template <int MG>
+template <int G>
 __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const Shared sh = carve(a, smem);
@@ -928,8 +1042,10 @@ __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs
     const Sched sc = make_sched(a, pos);
     if (warp == W) {
         producer(a, sh, sc, pos);
+    } else if (warp == W + 1) {
+        prefetcher(a, sh, sc, pos);
     } else {
-        consumer<MG>(a, sh, sc, pos);
+        consumer<G>(a, sh, sc, pos);
     }
     pdl_launch_dependents();
 }
@@ -1012,13 +1128,14 @@ size_t stack_kpart_floats(const StackArgs& a) {
 
 bool stack_plan(StackArgs* a, int grid) {
     const int G = a->kv_heads > 0 ? a->q_heads / a->kv_heads : 0;
-    if (a->L <= 0 || a->kv_heads <= 0 || a->q_heads % a->kv_heads || G < 1 || G > kStackMaxGroup || G + 1 > W) return false;
+    if (a->L <= 0 || a->kv_heads <= 0 || a->q_heads % a->kv_heads) return false;
+    if (G != 1 && G != 2 && G != 4 && G != 5 && G != 8) return false;  // instantiated group sizes
     if (a->q_dim != a->q_heads * 128 || a->kv_dim != a->kv_heads * 128) return false;
     if (a->inter % 8 || grid <= 0) return false;
     if (a->hidden > W * kStageRegs * 128) return false;  // the RMSNorm'ed input is staged in one batch
     const int nk[kStackPhases][2] = {{a->q_dim + 2 * a->kv_dim, a->hidden}, {0, 0}, {a->hidden, a->q_dim},
                                      {2 * a->inter, a->hidden}, {a->hidden, a->inter}};
-    int max_k = 0, max_units = 0, max_ipu = 0;
+    int max_k = 0, max_units = 0, max_part = 0;
     for (int p = 0; p < kStackPhases; ++p) {
         StackPhase& ph = a->ph[p];
         ph = StackPhase{};
@@ -1028,22 +1145,24 @@ bool stack_plan(StackArgs* a, int grid) {
         if (ph.n % kItemRows || ph.k % kItemK || ph.k <= 0) return false;
         ph.tiles = ph.n / kItemRows;
         ph.ipr = ph.k / kItemK;
+        // K split only when a whole row tile exceeds 64 items (split-K partials cost a
+        // ticket round trip; rotation already balances the bytes per CTA over a layer)
         ph.kparts = 1;
-        while (ph.ipr / ph.kparts > 16 || ph.ipr % ph.kparts) ++ph.kparts;
+        while (ph.ipr / ph.kparts > 64 || ph.ipr % ph.kparts) ++ph.kparts;
         ph.ipu = ph.ipr / ph.kparts;
         ph.units = ph.tiles * ph.kparts;
         max_k = std::max(max_k, ph.k);
         max_units = std::max(max_units, (ph.units + grid - 1) / grid);
-        max_ipu = std::max(max_ipu, ph.ipu);
+        max_part = std::max(max_part, ((ph.units + grid - 1) / grid) * ph.ipu * 16);
     }
     a->grid = grid;
     a->max_units = max_units;
-    a->part_stride = max_ipu * 16;
+    a->part_floats = max_part;  // one 16-row slot per item of every unit of a phase
     a->max_chunks = (a->capacity + kStackChunk - 1) / kStackChunk;
     const int digits = (max_k / 128) * (512 + 8);
-    const int att = (G * 128 + 256 + 2 * W * kStackMaxGroup + 2 * kStackMaxGroup + W * G * 128 + G * a->max_chunks) * 4;
+    const int att = (G * 128 + 256 + 3 * W * kStackMaxGroup + 2 * kStackMaxGroup + W * G * 128 + G * a->max_chunks) * 4;
     const int xbytes = align_up(std::max(digits, att), 128);
-    const int part = align_up(max_units * a->part_stride * 4, 16);
+    const int part = align_up(a->part_floats * 4, 16);
     const int ucnt = align_up(max_units * 4, 16);
     const int misc = 32 * 4 + 32;
     const int fixed = xbytes + part + ucnt + misc + 256;
@@ -1068,8 +1187,15 @@ bool stack_plan(StackArgs* a, int grid) {
 }
 
 cudaError_t stack_launch(const StackArgs& a, cudaStream_t s, bool cooperative) {
-    const int G = a.q_heads / a.kv_heads;
-    auto kern = G <= 2 ? stack_kernel<2> : (G <= 4 ? stack_kernel<4> : stack_kernel<8>);
+    void (*kern)(const StackArgs) = nullptr;
+    switch (a.q_heads / a.kv_heads) {
+    case 1: kern = stack_kernel<1>; break;
+    case 2: kern = stack_kernel<2>; break;
+    case 4: kern = stack_kernel<4>; break;
+    case 5: kern = stack_kernel<5>; break;
+    case 8: kern = stack_kernel<8>; break;
+    default: return cudaErrorInvalidValue;
+    }
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, a.smem_bytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};

@@ -5,7 +5,8 @@
 // Every INT4 projection is stored as "items" of 16 rows x 256 K (2208 bytes) in the
 // order the kernel reads them. One CTA runs per SM: a producer warp streams every item
 // the CTA will consume in this step (all layers, all phases, plus the attention K/V
-// rows) into a shared-memory ring with TMA bulk copies, while 16 consumer warps run the
+// rows) into a shared-memory ring with TMA bulk copies (a second warp walks the same
+// sequence further ahead with L2 bulk prefetches), while 16 consumer warps run the
 // phases qkv -> attention -> o -> gate/up -> down of each layer. A phase waits on a
 // device-wide counter of the CTAs that finished the phase it depends on; the weight
 // stream does not wait, so HBM stays busy across phase boundaries.
@@ -25,11 +26,13 @@ constexpr int kItemScaleOff = 2048;
 constexpr int kItemZeroOff = 2176;
 constexpr int kStackPhases = 5;  // 0 qkv, 1 attention, 2 o, 3 gate/up, 4 down
 constexpr int kStackConsumerWarps = 16;
-constexpr int kStackThreads = (kStackConsumerWarps + 1) * 32;
+// consumer warps, the ring producer warp and the L2 prefetch warp
+constexpr int kStackThreads = (kStackConsumerWarps + 2) * 32;
+constexpr int kStackPrefetchAhead = 150;  // items the L2 prefetcher runs ahead of the ring
 constexpr int kStackChunk = 128;  // keys per attention unit
 constexpr int kStackMaxGroup = 8;  // q heads per KV head
 constexpr int kStackErrTimeout = 3;  // DecodeState::error when a bounded wait gave up
-constexpr int kStackTraceSlots = 7;
+constexpr int kStackTraceSlots = 13;
 
 enum StackPackMode : int { kPackRows = 0, kPackGateUp = 1 };
 
@@ -88,14 +91,16 @@ struct StackArgs {
     // 0 phase entered, 1 input dependency met, 2 input staged, 3 the CTA's last unit
     // done, 4 the producer issued the phase's last item (0 where the CTA had no units);
     // then SM cycles: 5 consumer warps waiting for ring items (summed over warps),
-    // 6 the producer waiting for free slots
+    // 6 the producer waiting for free slots; attention only (first unit of the CTA),
+    // stamps: 2 q/k prepared, 7 chunk partial written, 8 ticket taken, 9 merge done,
+    // and warp 0's own progress: 10 scores done, 11 local softmax done, 12 P.V done
     unsigned long long* trace;
     StackPhase ph[kStackPhases];  // index 1 (attention) unused
     // shared-memory plan (filled by stack_plan)
     int grid;
     int ring_slots;
     int max_units;    // GEMV units one CTA owns in one phase, at most
-    int part_stride;  // floats per unit partial slot (max ipu * 16)
+    int part_floats;  // floats of the per-item partial sums of one phase (max over phases)
     int off_bar, off_x, off_part, off_ucnt, off_misc;
     int smem_bytes;
 };

@@ -138,8 +138,15 @@ class Qwen3Engine:
     def kernels_per_step(self) -> int:
         return self._L.fire_b200_qwen3_kernels_per_step(self._h)
 
+    def time_layer_stack(self, reps: int = 5, stream=None) -> float:
+        """Average device milliseconds of one launch of the layer-stack kernel alone."""
+        ms = C.c_float(0.0)
+        N.check(self._L.fire_b200_qwen3_time_layer_stack(self._h, int(reps), C.byref(ms), N.stream_handle(stream)),
+                "time_layer_stack")
+        return float(ms.value)
+
     def stack_trace(self) -> np.ndarray:
-        """Per-phase timeline of the last layer-stack launch, [CTAs, layers, 5, 7] stamps
+        """Per-phase timeline of the last layer-stack launch, [CTAs, layers, 5, 13] values
         (empty unless FIRE_B200_STACK_TRACE=1 was set when the engine was created)."""
         n = int(self._L.fire_b200_qwen3_stack_trace(self._h, None, 0))
         if n <= 0:
@@ -148,7 +155,7 @@ class Qwen3Engine:
         got = int(self._L.fire_b200_qwen3_stack_trace(self._h, out.ctypes.data, n))
         if got < 0:
             raise N.FireB200Error(got, "stack trace read failed")
-        return out.reshape(-1, self.profile.num_layers, 5, 7)
+        return out.reshape(-1, self.profile.num_layers, 5, 13)
 
     @property
     def step_weight_bytes(self) -> int:

@@ -91,13 +91,19 @@ int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m);
 
 /* Diagnostics (no reference counterpart): with FIRE_B200_STACK_TRACE=1 in the
  * environment at create time, the persistent layer-stack kernel records a per-phase
- * timeline of its last launch, [CTAs][layers][5 phases][7 values]: 5 stamps of the
+ * timeline of its last launch, [CTAs][layers][5 phases][13 values]: 5 stamps of the
  * GPU's nanosecond timer (phase entered, input ready, input staged, last unit done, last
  * item issued) and 2 SM-cycle totals (consumer warps waiting for ring items, the
- * producer waiting for free slots). Copies up to capacity_words words into out (may be
+ * producer waiting for free slots), then 6 attention stamps (chunk partial written,
+ * ticket taken, merge done; warp 0's scores, local softmax and P.V done). Copies up to capacity_words words into out (may be
  * NULL) after a device synchronisation; returns the word count, 0 when tracing is off,
  * -1 on a CUDA error. */
 int64_t fire_b200_qwen3_stack_trace(const fire_b200_qwen3* m, uint64_t* out, int64_t capacity_words);
+/* Diagnostics: average device time in milliseconds of `reps` launches of the layer-stack
+ * kernel alone at position length() (its KV row is rewritten, the length is unchanged),
+ * timed with CUDA events on `stream` (NULL = default). FIRE_B200_ERR_STATE when the
+ * engine does not use the layer-stack kernel (tensor parallel, or switched off). */
+int fire_b200_qwen3_time_layer_stack(fire_b200_qwen3* m, int reps, float* ms_out, void* stream);
 /* Weight bytes one decode step reads on this rank (projections, head, norms, one
  * embedding row): the numerator of the HBM roofline. */
 uint64_t fire_b200_qwen3_step_weight_bytes(const fire_b200_qwen3* m);
