@@ -54,6 +54,8 @@ def parse():
     # profiling knobs (defaults are the measured workload)
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled once")
     ap.add_argument("--gen", type=int, default=GEN, help="greedy tokens per step")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers (0 = the model's 36); fewer only to size an ncu capture")
     return ap.parse_args()
 
 
@@ -292,6 +294,10 @@ def run_ours(args):
         dist.broadcast_object_list(obj, src=0)
         nid = obj[0]
     p = QWEN3_8B
+    if args.layers:
+        import dataclasses
+
+        p = dataclasses.replace(p, num_layers=args.layers)
     w = synth.generate_torch(p, "mixed", seed=0, device="cuda")
     eng = Qwen3Engine(p, w, tp_rank=rank, tp_size=world, nccl_id=nid)
     cpu_w = None
@@ -392,7 +398,8 @@ def run_ours(args):
             "config": {"workload": "qwen3-8b-w4-decode-ctx2048", "model": "Qwen3-8B (random init)",
                        "layout": "mixed: INT4 g128 projections, BF16 embedding/head, FP32 norms/activations/KV",
                        "prompt": n_prompt, "generated_per_step": n_gen, "context": n_prompt + n_gen,
-                       "parallelism": f"tp{world}", "l2": "weights 4.99 GB/token > 126 MB L2 (no flush needed)"},
+                       "parallelism": f"tp{world}", "layers": p.num_layers,
+                       "l2": "weights 4.99 GB/token > 126 MB L2 (no flush needed)"},
             "e2e": {"value": tok_s_e2e, "unit": "tok/s", "h2d_bytes_per_step": 16 * n_gen,
                     "d2h_bytes_per_step": 4 * n_gen},
             "gpu_launches": (eng.kernels_per_step * n_gen + 1) * args.steps,
