@@ -1,0 +1,90 @@
+"""Tensor-parallel decode on 2 (or 4) GPUs, one process per GPU, NCCL between them.
+
+Each rank builds the engine with its shard (column-parallel q/k/v and gate/up, row-parallel
+o/down, vocab-sharded head, KV heads by rank) and runs the same steps; the all-gathered
+logits of every rank must match the unsharded oracle (src/model/qwen.cpp:155-303) within
+the model-level bar, the ranks must agree bit for bit, and the device greedy loop must
+produce the oracle's tokens. Skipped when fewer GPUs are visible.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from fire_b200 import synth
+from fire_b200.profiles import Qwen3Profile
+
+pytestmark = pytest.mark.gpu
+
+# heads, FFN width and vocab divide by 4; K slices stay group aligned
+P = Qwen3Profile("tp-gpu", 4096, 512, 512, 1536, 2, 8, 4, 128)
+PROMPT = [11, 2024, 7, 99, 3000, 5, 17]
+STEPS = 24
+
+
+def _rank(rank, world, nid, w, q):
+    try:
+        torch.cuda.set_device(rank)
+        from fire_b200.engine import Qwen3Engine
+
+        eng = Qwen3Engine(P, w, tp_rank=rank, tp_size=world, nccl_id=nid)
+        eng.prepare(64)
+        logits = torch.empty(P.vocab_size, device="cuda")
+        got = []
+        for i, t in enumerate(PROMPT):
+            eng.forward(t, i, logits)
+            torch.cuda.synchronize()
+            got.append(logits.cpu().numpy().copy())
+        eng.reset()
+        for i, t in enumerate(PROMPT[:-1]):
+            eng.forward(t, i)
+        toks = eng.generate(PROMPT[-1], STEPS).cpu().tolist()
+        torch.cuda.synchronize()
+        eng.close()
+        q.put((rank, np.stack(got), toks, None))
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, None, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_decode_matches_oracle(cuda, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from fire_b200.engine import nccl_unique_id
+    from oracle import oracle as O
+
+    w = synth.generate(P, "mixed", seed=11)
+    nid = nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, w, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, logits, toks, err = q.get(timeout=600)
+        assert err is None, f"rank {rank}: {err}"
+        res[rank] = (logits, toks)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = O.Qwen3Oracle(P, w, capacity=64)
+    want_logits = [ref.forward(t, i) for i, t in enumerate(PROMPT)]
+    lg = want_logits[-1]
+    want = []
+    for i in range(STEPS):
+        nxt = O.argmax(lg)
+        want.append(nxt)
+        lg = ref.forward(nxt, len(PROMPT) + i)
+    for r in range(world):
+        got, toks = res[r]
+        assert np.array_equal(got, res[0][0]), f"rank {r} logits differ from rank 0"
+        for i in range(len(PROMPT)):
+            g, e = got[i], want_logits[i]
+            rel = float(np.linalg.norm(g - e) / np.linalg.norm(e))
+            assert rel < 1e-4, (i, rel)
+            assert float(np.max(np.abs(g - e))) < 1e-2
+            assert int(np.argmax(g)) == int(np.argmax(e))
+        assert toks == want, (r, toks, want)
