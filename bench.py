@@ -54,6 +54,8 @@ def parse():
     # profiling knobs (defaults are the measured workload)
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens prefilled once")
     ap.add_argument("--gen", type=int, default=GEN, help="greedy tokens per step")
+    ap.add_argument("--prefill", action="store_true",
+                    help="only the M=512 INT4 prefill GEMM sweep over the 8B projection shapes")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers (0 = the model's 36); fewer only to size an ncu capture")
     return ap.parse_args()
@@ -260,6 +262,57 @@ def time_w4_gemv(stream, reps: int = 4):
     return by / launches, ms * 1e3 / launches  # bytes per launch, us per launch
 
 
+PREFILL_M = 512
+PREFILL_SHAPES = [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)]  # q/k/v, o, gate/up, down
+
+
+def prefill_sweep(reps: int = 10):
+    """The tensor-core INT4 prefill Linear (fire_b200_linear_w4_prefill) at M = 512 on every
+    Qwen3-8B projection shape, timed with CUDA events per call (dequant + split + GEMM)."""
+    import torch
+
+    from fire_b200 import _native as N
+
+    L = N.lib()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    out, tot_fl, tot_us = [], 0.0, 0.0
+    for n, k in PREFILL_SHAPES:
+        x = torch.randn(PREFILL_M, k, device="cuda", generator=g)
+        q = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device="cuda", generator=g)
+        s = torch.rand(n, k // 128, device="cuda", generator=g) * 0.02
+        z = torch.randint(0, 16, (n, k // 128), dtype=torch.uint8, device="cuda", generator=g)
+        y = torch.empty(PREFILL_M, n, device="cuda")
+        wsb = L.fire_b200_linear_w4_prefill_workspace_bytes(PREFILL_M, n, k)
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        stream = torch.cuda.current_stream()
+
+        def call():
+            rc = L.fire_b200_linear_w4_prefill(x.data_ptr(), q.data_ptr(), s.data_ptr(), z.data_ptr(), y.data_ptr(),
+                                               PREFILL_M, n, k, 128, ws.data_ptr(), wsb, st.data_ptr(),
+                                               stream.cuda_stream)
+            assert rc == 0, rc
+
+        for _ in range(3):
+            call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        fl = 2.0 * PREFILL_M * n * k
+        tot_fl += fl
+        tot_us += us
+        out.append({"n": n, "k": k, "us": round(us, 1), "tflops": round(fl / us / 1e6, 1)})
+        del x, q, s, z, y, ws
+    return {"m": PREFILL_M, "shapes": out, "sweep_tflops": round(tot_fl / tot_us / 1e6, 1),
+            "note": "per call: W dequant to BF16 + x hi/lo split + tcgen05 GEMM (2 BF16 MMAs per K16)"}
+
+
 def layer_stack_bytes(p, world: int, pos: int) -> float:
     """Algorithmic HBM bytes of one layer-stack launch at position `pos`: per layer the
     INT4 q/k/v, o, gate/up and down matrices (0.5 B per weight, 4 B scale + 1 B zero point
@@ -415,6 +468,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if world == 1:
+            line["prefill"] = prefill_sweep()
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:
@@ -426,6 +481,13 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.prefill:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"metric": "INT4 prefill GEMM TFLOP/s (M=512, Qwen3-8B projection shapes)",
+                          **prefill_sweep()}), flush=True)
+        return 0
     return run_ours(args)
 
 

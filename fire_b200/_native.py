@@ -34,6 +34,8 @@ SIGNATURES: Dict[str, tuple] = {
     "fire_b200_abi_version": (_i, []),
     "fire_b200_status_string": (C.c_char_p, [_i]),
     "fire_b200_linear_w4": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "fire_b200_linear_w4_prefill_workspace_bytes": (C.c_size_t, [_i, _i, _i]),
+    "fire_b200_linear_w4_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, C.c_size_t, _vp, _vp]),
     "fire_b200_linear_dense": (_i, [_vp, _vp, _i, _f, _vp, _i, _i, _i, _vp]),
     "fire_b200_rmsnorm": (_i, [_vp, _vp, _vp, _i, _f, _vp]),
     "fire_b200_rmsnorm_rows": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),

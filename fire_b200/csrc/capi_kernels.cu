@@ -11,6 +11,7 @@
 #include "kernels/dense_gemv.h"
 #include "kernels/ops.h"
 #include "kernels/w4_gemv.h"
+#include "kernels/w4_prefill.h"
 
 namespace {
 
@@ -61,6 +62,35 @@ int fire_b200_linear_w4(const float* x, const uint8_t* qweight, const float* sca
     }
     return rc(fb::w4_linear_generic_launch(x, qweight, scales, zero_points, y, rows, n, k,
                                            group_size, sms, S(stream)));
+}
+
+namespace {
+__device__ int g_prefill_status;  // status word for callers that pass none
+}  // namespace
+
+size_t fire_b200_linear_w4_prefill_workspace_bytes(int rows, int n, int k) {
+    if (rows < 1 || n < 1 || k < 1) return 0;
+    return fb::prefill_workspace_bytes(rows, n, k);
+}
+
+int fire_b200_linear_w4_prefill(const float* x, const uint8_t* qweight, const float* scales,
+                                const uint8_t* zero_points, float* y, int rows, int n, int k,
+                                int group_size, void* workspace, size_t workspace_bytes,
+                                int* status_dev, void* stream) {
+    if (!x || !qweight || !scales || !zero_points || !y || !workspace) return FIRE_B200_ERR_INVALID;
+    if (!fb::prefill_supported(rows, n, k, group_size)) return FIRE_B200_ERR_UNSUPPORTED;
+    if (workspace_bytes < fb::prefill_workspace_bytes(rows, n, k)) return FIRE_B200_ERR_INVALID;
+    if (!aligned(x, 16) || !aligned(y, 16) || !aligned(workspace, 16) || !aligned(qweight, 4) ||
+        !aligned(scales, 4))
+        return FIRE_B200_ERR_INVALID;
+    int* st = status_dev;
+    if (st == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_prefill_status) != cudaSuccess) return FIRE_B200_ERR_STATE;
+        st = static_cast<int*>(p);
+    }
+    return rc(fb::prefill_w4_launch(x, qweight, scales, zero_points, y, rows, n, k, workspace, workspace_bytes,
+                                    st, S(stream)));
 }
 
 int fire_b200_linear_dense(const float* x, const void* weight, int weight_dtype, float scale,

@@ -1,0 +1,23 @@
+// INT4 group-128 Linear for many rows (prefill, M >= 64) on the 5th-generation tensor
+// cores: Y[M, N] = X[M, K] . dequant(W)[N, K]^T, FP32 in and out, BF16 operands, FP32
+// accumulation in tensor memory. Replaces matmul_quant_int4_fp32_naive for rows > 1
+// (src/op/kernels/cuda/matmul_kernel.cu:202-227, dispatched from :280-314).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fb {
+
+constexpr int kPrefillBM = 128;  // rows of X per CTA tile (UMMA M)
+constexpr int kPrefillBN = 128;  // rows of W per CTA tile (UMMA N)
+constexpr int kPrefillBK = 64;   // K per pipeline stage (one 128-byte swizzle row of BF16)
+
+// Shapes the tensor-core path takes: M % 128 == 0, N % 128 == 0, K % 128 == 0, group 128.
+bool prefill_supported(int M, int N, int K, int group);
+// Scratch: BF16 x_hi and x_lo [M, K] and the dequantised W [N, K].
+size_t prefill_workspace_bytes(int M, int N, int K);
+cudaError_t prefill_w4_launch(const float* x, const uint8_t* qw, const float* scales, const uint8_t* zeros, float* y,
+                              int M, int N, int K, void* workspace, size_t workspace_bytes, int* err,
+                              cudaStream_t s);
+
+}  // namespace fb

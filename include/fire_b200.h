@@ -63,6 +63,21 @@ int fire_b200_linear_w4(const float* x, const uint8_t* qweight, const float* sca
                         const uint8_t* zero_points, float* y, int rows, int n, int k,
                         int group_size, void* stream);
 
+/* INT4 group-128 Linear for many rows (prefill, M >= 128) on the tcgen05 tensor cores.
+ * Replaces matmul_quant_int4_fp32_naive for rows > 1 (src/op/kernels/cuda/matmul_kernel.cu:
+ * 202-227, dispatched from :280-314). Same arguments and meaning as fire_b200_linear_w4,
+ * but the product is taken on BF16 tensor cores: each weight s * (q - z) rounded once to
+ * BF16, x as the sum of two BF16 terms (x_hi + x_lo), FP32 accumulation. Requires rows % 128 == 0,
+ * n % 128 == 0, k % 128 == 0, group_size == 128, 16-byte aligned x, y and workspace.
+ * workspace: at least fire_b200_linear_w4_prefill_workspace_bytes(rows, n, k) bytes of
+ * device memory (x_hi, x_lo and the dequantised BF16 weights). status_dev: optional device int that a bounded wait
+ * sets non-zero if it gives up (NULL: a word inside the library). */
+size_t fire_b200_linear_w4_prefill_workspace_bytes(int rows, int n, int k);
+int fire_b200_linear_w4_prefill(const float* x, const uint8_t* qweight, const float* scales,
+                                const uint8_t* zero_points, float* y, int rows, int n, int k,
+                                int group_size, void* workspace, size_t workspace_bytes,
+                                int* status_dev, void* stream);
+
 /* Dense Linear, FP32 or BF16 weights widened to FP32: y = scale * x W^T.
  * Replaces kernel::matmul_kernel_cu (src/op/kernels/cuda/matmul_kernel.cu:146-199)
  * reached from LinearOp::forward (src/op/linear.cpp:27-29); the LM head at M = 1.
