@@ -397,9 +397,13 @@ __device__ __forceinline__ Slot slot_of(unsigned seq, int S) {
 __device__ bool wait_item(const StackArgs& a, const Shared& sh, Slot sl, long long& waited) {
     const unsigned parity = sl.parity;
     uint64_t* b = &sh.full[sl.index];
-    if (__all_sync(0xffffffffu, mbar_try(b, parity))) return true;  // common case: already landed
-    if (__any_sync(0xffffffffu, failed(sh))) return false;
+    // (try_wait may itself block for a while, so the traced time starts before it)
     const long long c0 = a.trace != nullptr ? clock64() : 0;
+    if (__all_sync(0xffffffffu, mbar_try(b, parity))) {  // common case: already landed
+        if (a.trace != nullptr) waited += clock64() - c0;
+        return true;
+    }
+    if (__any_sync(0xffffffffu, failed(sh))) return false;
     const unsigned long long t0 = gtime();
     bool ok = false;
     for (int i = 0; i < kSpinLimit; ++i) {
@@ -678,27 +682,45 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
     float res0 = 0.0f;
     if (resid != nullptr && warp < count && lane < 16)
         res0 = __ldcg(resid + ((first + warp * sc.grid) / ph.kparts) * 16 + lane);
+    // this warp's items s = warp, warp + W, ...: unit k, item j, ring slot and parity all
+    // advance incrementally (no division per item; W < ring slots)
+    const int S = a.ring_slots;
+    int k = warp / ph.ipu, j = warp % ph.ipu;
+    Slot sl = slot_of(seq_base + static_cast<unsigned>(warp), S);
+    int kp = ph.kparts == 1 ? 0 : (first + k * sc.grid) % ph.kparts;
     for (int s = warp; s < total; s += W) {
-        const int k = s / ph.ipu, j = s % ph.ipu;
-        const Slot sl = slot_of(seq_base + static_cast<unsigned>(s), a.ring_slots);
-        if (!wait_item(a, sh, sl, waited)) continue;
-        const ItemRegs it = load_item(sh.ring + static_cast<size_t>(sl.index) * kItemBytes);
-        release_item(sh, sl);
-        const int kp = (first + k * sc.grid) % ph.kparts;
-        float acc0 = 0.0f, acc1 = 0.0f;
-        item_accumulate(it, sh, groups, 2 * (kp * ph.ipu + j), acc0, acc1);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-        if ((lane & 3) == 0) {
-            float* dst = sh.part + static_cast<size_t>(k) * ph.ipu * 16 + j * 16;
-            dst[lane >> 2] = acc0;
-            dst[(lane >> 2) + 8] = acc1;
+        if (wait_item(a, sh, sl, waited)) {
+            const ItemRegs it = load_item(sh.ring + static_cast<size_t>(sl.index) * kItemBytes);
+            release_item(sh, sl);
+            float acc0 = 0.0f, acc1 = 0.0f;
+            item_accumulate(it, sh, groups, 2 * (kp * ph.ipu + j), acc0, acc1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+            if ((lane & 3) == 0) {
+                float* dst = sh.part + (static_cast<size_t>(k) * ph.ipu + j) * 16;
+                dst[lane >> 2] = acc0;
+                dst[(lane >> 2) + 8] = acc1;
+            }
+        }
+        j += W;
+        bool new_unit = false;
+        while (j >= ph.ipu) {
+            j -= ph.ipu;
+            ++k;
+            new_unit = true;
+        }
+        if (new_unit && ph.kparts > 1) kp = (first + k * sc.grid) % ph.kparts;
+        sl.index += W;
+        if (sl.index >= S) {
+            sl.index -= S;
+            sl.parity ^= 1u;
         }
     }
     if (a.trace != nullptr && lane == 0 && waited > 0)
         atomicAdd(reinterpret_cast<unsigned long long*>(sh.misc + 4), static_cast<unsigned long long>(waited));
+    if (threadIdx.x == 0) stamp(a, l, p, 7);
     // all items of the phase are in: finish the units in parallel, then one thread
     // publishes the phase (barrier, then fence + counter: every epilogue store of this
     // CTA is ordered before the counter update)

@@ -93,7 +93,8 @@ struct StackArgs {
     // then SM cycles: 5 consumer warps waiting for ring items (summed over warps),
     // 6 the producer waiting for free slots; attention only (first unit of the CTA),
     // stamps: 2 q/k prepared, 7 chunk partial written, 8 ticket taken, 9 merge done,
-    // and warp 0's own progress: 10 scores done, 11 local softmax done, 12 P.V done
+    // and warp 0's own progress: 10 scores done, 11 local softmax done, 12 P.V done;
+    // GEMV phases: 7 warp 0's last item done (before the phase's finish step)
     unsigned long long* trace;
     StackPhase ph[kStackPhases];  // index 1 (attention) unused
     // shared-memory plan (filled by stack_plan)
