@@ -38,6 +38,7 @@ SIGNATURES: dict = {
     "fire_b200_qwen3_kernels_per_step": (_i, [_vp]),
     "fire_b200_qwen3_stack_trace": (C.c_int64, [_vp, _vp, C.c_int64]),
     "fire_b200_qwen3_time_layer_stack": (_i, [_vp, _i, C.POINTER(C.c_float), _vp]),
+    "fire_b200_qwen3_prefill": (_i, [_vp, _vp, _i, _vp, _vp]),
     "fire_b200_qwen3_step_weight_bytes": (C.c_uint64, [_vp]),
     "fire_b200_qwen3_destroy": (None, [_vp]),
 }

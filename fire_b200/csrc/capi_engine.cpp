@@ -140,6 +140,10 @@ int fire_b200_qwen3_truncate(fire_b200_qwen3* m, int length) {
 int fire_b200_qwen3_length(const fire_b200_qwen3* m) { return m ? m->e->length() : -1; }
 const float* fire_b200_qwen3_logits(const fire_b200_qwen3* m) { return m ? m->e->logits() : nullptr; }
 int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m) { return m ? m->e->kernels_per_step() : 0; }
+int fire_b200_qwen3_prefill(fire_b200_qwen3* m, const int32_t* tokens, int n, float* logits_out, void* stream) {
+    if (m == nullptr) return FIRE_B200_ERR_INVALID;
+    return m->e->prefill(tokens, n, logits_out, static_cast<cudaStream_t>(stream));
+}
 int fire_b200_qwen3_time_layer_stack(fire_b200_qwen3* m, int reps, float* ms_out, void* stream) {
     if (m == nullptr) return FIRE_B200_ERR_INVALID;
     return m->e->time_layer_stack(reps, ms_out, static_cast<cudaStream_t>(stream));

@@ -10,7 +10,9 @@
 #include "fire_b200.h"
 #include "kernels/dense_gemv.h"
 #include "kernels/ops.h"
+#include "kernels/prefill_ops.h"
 #include "kernels/w4_gemv.h"
+#include "kernels/w4_prefill.h"
 
 namespace fb {
 
@@ -714,6 +716,150 @@ int Qwen3Engine::forward(int token, int pos, float* logits_out, cudaStream_t s) 
         FB_CK(cudaMemcpyAsync(logits_out, logits(), size_t(d_.vocab) * 4, cudaMemcpyDeviceToDevice, s));
     ++length_;  // KVCache::commit (src/model/kv_cache.cpp:76-83)
     return 0;
+}
+
+namespace {
+constexpr int kPrefillChunk = 512;    // prompt rows per batched step
+constexpr int kPrefillMinRows = 64;   // below this the per-token path is as fast
+}  // namespace
+
+int Qwen3Engine::prefill_buffers() {
+    if (prefill_arena_) return 0;
+    const size_t C = kPrefillChunk, H = d_.hidden;
+    const size_t qkv = size_t(q_ + 2 * kv_), maxk = std::max({size_t(H), size_t(q_), size_t(f_)});
+    const size_t maxw = std::max({qkv * H, size_t(H) * q_, size_t(2 * f_) * H, size_t(H) * f_}) * 2;
+    pf_gemm_ws_bytes_ = prefill_gemm_workspace_bytes(kPrefillChunk, static_cast<int>(maxk));
+    std::unique_ptr<DeviceArena> ar(new DeviceArena(device_));
+    const size_t sizes[] = {C * 4, C * H * 4, C * H * 4, C * qkv * 4, C * q_ * 4, C * q_ * 4, C * H * 4,
+                            C * 2 * f_ * 4, C * f_ * 4, pf_gemm_ws_bytes_, maxw, 256};
+    size_t total = 0;
+    for (size_t z : sizes) total += pad256(z) + 256;
+    FB_RC(ar->reserve(total));
+    pf_tok_ = static_cast<int32_t*>(ar->alloc(C * 4));
+    pf_x_ = static_cast<float*>(ar->alloc(C * H * 4));
+    pf_xn_ = static_cast<float*>(ar->alloc(C * H * 4));
+    pf_qkv_ = static_cast<float*>(ar->alloc(C * qkv * 4));
+    pf_q_ = static_cast<float*>(ar->alloc(C * q_ * 4));
+    pf_att_ = static_cast<float*>(ar->alloc(C * q_ * 4));
+    pf_o_ = static_cast<float*>(ar->alloc(C * H * 4));
+    pf_gu_ = static_cast<float*>(ar->alloc(C * 2 * f_ * 4));
+    pf_act_ = static_cast<float*>(ar->alloc(C * f_ * 4));
+    pf_gemm_ws_ = ar->alloc(pf_gemm_ws_bytes_);
+    pf_w_ = ar->alloc(maxw);
+    pf_err_ = static_cast<int*>(ar->alloc(256));
+    if (!pf_tok_ || !pf_x_ || !pf_xn_ || !pf_qkv_ || !pf_q_ || !pf_att_ || !pf_o_ || !pf_gu_ || !pf_act_ ||
+        !pf_gemm_ws_ || !pf_w_ || !pf_err_)
+        return FIRE_B200_ERR_NOMEM;
+    FB_CK(cudaMemset(pf_err_, 0, 256));
+    prefill_arena_ = std::move(ar);
+    return 0;
+}
+
+// y[mp, n] = x[mp, k] . W^T for a layer-stack item matrix W (dequantised into BF16 first)
+int Qwen3Engine::prefill_linear(const float* x, const uint8_t* items, int n, int k, float* y, int mp,
+                                cudaStream_t s) {
+    FB_CK(prefill_dequant_items_launch(items, n, k, pf_w_, s));
+    FB_CK(prefill_gemm_launch(x, pf_w_, y, mp, n, k, pf_gemm_ws_, pf_gemm_ws_bytes_, pf_err_, s));
+    return 0;
+}
+
+int Qwen3Engine::prefill_chunk(int m, int mp, int pos0, cudaStream_t s) {
+    const int H = d_.hidden;
+    FB_CK(embedding_launch(pf_tok_, m, nullptr, embedding_, emb_bf16_, d_.vocab, H, pf_x_, s, false));
+    if (mp > m) {
+        FB_CK(cudaMemsetAsync(pf_x_ + size_t(m) * H, 0, size_t(mp - m) * H * 4, s));
+        FB_CK(cudaMemsetAsync(pf_att_ + size_t(m) * q_, 0, size_t(mp - m) * q_ * 4, s));
+    }
+    for (int l = 0; l < d_.layers; ++l) {
+        const Layer& L = layers_[l];
+        // q/k/v = W_qkv . rmsnorm(x) for every row (qwen.cpp:196-217)
+        FB_CK(rmsnorm_rows_launch(pf_x_, L.attn_norm, pf_xn_, mp, H, d_.eps, s));
+        FB_RC(prefill_linear(pf_xn_, L.qkv_items, q_ + 2 * kv_, H, pf_qkv_, mp, s));
+        // q/k norm + RoPE, KV write (qwen.cpp:222-240), causal attention (qwen.cpp:242-247)
+        PrefillRowsArgs pa{};
+        pa.n = m;
+        pa.pos0 = pos0;
+        pa.q_heads = hq_;
+        pa.kv_heads = hkv_;
+        pa.eps = d_.eps;
+        pa.scale = 1.0f / sqrtf(128.0f);
+        pa.qkv = pf_qkv_;
+        pa.q_norm = L.q_norm;
+        pa.k_norm = L.k_norm;
+        pa.rope_sin = rope_sin_;
+        pa.rope_cos = rope_cos_;
+        pa.q_out = pf_q_;
+        pa.kcache = kcache_ + size_t(l) * capacity_ * kv_;
+        pa.vcache = vcache_ + size_t(l) * capacity_ * kv_;
+        pa.attn_out = pf_att_;
+        FB_CK(qk_rope_kv_rows_launch(pa, s));
+        FB_CK(causal_attention_launch(pa, s));
+        // o projection + residual (qwen.cpp:249-262)
+        FB_RC(prefill_linear(pf_att_, L.o_items, H, q_, pf_o_, mp, s));
+        FB_CK(add_launch(pf_x_, pf_o_, pf_x_, mp * H, sms_, s));
+        // SwiGLU FFN + residual (qwen.cpp:264-291)
+        FB_CK(rmsnorm_rows_launch(pf_x_, L.ffn_norm, pf_xn_, mp, H, d_.eps, s));
+        FB_RC(prefill_linear(pf_xn_, L.gu_items, 2 * f_, H, pf_gu_, mp, s));
+        FB_CK(swiglu_packed_rows_launch(pf_gu_, pf_act_, mp, f_, sms_, s));
+        FB_RC(prefill_linear(pf_act_, L.down_items, H, f_, pf_o_, mp, s));
+        FB_CK(add_launch(pf_x_, pf_o_, pf_x_, mp * H, sms_, s));
+    }
+    return 0;
+}
+
+int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaStream_t s) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (tokens == nullptr || n <= 0 || length_ + n > capacity_) return FIRE_B200_ERR_INVALID;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= d_.vocab) return FIRE_B200_ERR_INVALID;
+    if (!stack_ || tp_ > 1 || n < kPrefillMinRows) {
+        for (int i = 0; i < n; ++i) FB_RC(forward(tokens[i], length_, i == n - 1 ? logits_out : nullptr, s));
+        return 0;
+    }
+    FB_RC(prefill_buffers());
+    int done = 0, last_m = 0;
+    while (done < n) {
+        const int m = std::min(kPrefillChunk, n - done);
+        const int mp = (m + kPrefillBM - 1) / kPrefillBM * kPrefillBM;
+        FB_CK(cudaMemcpyAsync(pf_tok_, tokens + done, size_t(m) * 4, cudaMemcpyHostToDevice, s));
+        FB_RC(prefill_chunk(m, mp, length_, s));
+        FB_CK(cudaStreamSynchronize(s));  // the token buffer is reused by the next chunk
+        length_ += m;
+        done += m;
+        last_m = m;
+    }
+    // final norm + LM head on the last row (qwen.cpp:294-301)
+    const float* hx = pf_x_ + size_t(last_m - 1) * d_.hidden;
+    if (head_kind_ == 2) {
+        W4Args h{};
+        h.x = hx;
+        h.norm_w = final_norm_;
+        h.eps = d_.eps;
+        h.qw = head_w4_.qw;
+        h.scales = head_w4_.s;
+        h.zeros = head_w4_.z;
+        h.N = head_w4_.n;
+        h.K = head_w4_.k;
+        h.y = logits_;
+        FB_CK(w4g128_gemv_launch(h, kW4Store, sms_, s, false));
+    } else {
+        DenseArgs h{};
+        h.x = hx;
+        h.norm_w = final_norm_;
+        h.eps = d_.eps;
+        h.w = head_dense_;
+        h.scale = 1.0f;
+        h.y = logits_;
+        h.N = v_;
+        h.K = d_.hidden;
+        FB_CK(dense_gemv_launch(h, head_kind_ == 1, sms_, s, false));
+    }
+    if (logits_out != nullptr && logits_out != logits())
+        FB_CK(cudaMemcpyAsync(logits_out, logits(), size_t(d_.vocab) * 4, cudaMemcpyDeviceToDevice, s));
+    int err = 0;
+    FB_CK(cudaMemcpyAsync(&err, pf_err_, 4, cudaMemcpyDeviceToHost, s));
+    FB_CK(cudaStreamSynchronize(s));
+    return err == 0 ? 0 : FIRE_B200_ERR_STATE;
 }
 
 int Qwen3Engine::generate(int first_token, int steps, int32_t* tokens_out, cudaStream_t s) {

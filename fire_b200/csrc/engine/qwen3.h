@@ -82,6 +82,12 @@ class Qwen3Engine {
     // stream synchronisation. Prompt tokens are consumed first (no sampling until the
     // last one); out_host receives `steps` sampled ids.
     int generate_host(const int32_t* prompt, int n_prompt, int steps, int32_t* out_host, cudaStream_t s);
+    // Batched prefill: consume n prompt tokens (host ids) at positions length()..,
+    // leaving the KV cache and the last token's logits as n forward() calls would, with
+    // the projections on the tensor cores (BF16 operands, x as two BF16 terms). Falls back
+    // to forward() per token at tensor-parallel size > 1, with the per-op kernels, or for
+    // fewer than 64 tokens. Synchronises with `s` at the end (the host token copy).
+    int prefill(const int32_t* tokens, int n, float* logits_out, cudaStream_t s);
     int reset();
     int truncate(int length);
 
@@ -110,6 +116,9 @@ class Qwen3Engine {
     StackArgs stack_template(int capacity) const;
     int import_weights(const std::vector<TensorSrc>& tensors, std::string* err);
     int enqueue_step(cudaStream_t s, bool sample);
+    int prefill_buffers();
+    int prefill_chunk(int m, int mp, int pos0, cudaStream_t s);
+    int prefill_linear(const float* x, const uint8_t* items, int n, int k, float* y, int mp, cudaStream_t s);
     int capture(bool sample, cudaGraphExec_t* exec);
     int capture_once(bool sample, cudaGraphExec_t* exec);
     int launch_step(cudaStream_t s, bool sample);
@@ -163,6 +172,15 @@ class Qwen3Engine {
     StackArgs stack_args_{};
     unsigned* stack_sync_ = nullptr;
     size_t stack_sync_bytes_ = 0;
+    // batched prefill scratch (allocated on first use)
+    std::unique_ptr<DeviceArena> prefill_arena_;
+    int32_t* pf_tok_ = nullptr;
+    float *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_att_ = nullptr;
+    float *pf_o_ = nullptr, *pf_gu_ = nullptr, *pf_act_ = nullptr;
+    void* pf_gemm_ws_ = nullptr;
+    size_t pf_gemm_ws_bytes_ = 0;
+    void* pf_w_ = nullptr;  // BF16 copy of the matrix being multiplied
+    int* pf_err_ = nullptr;
     bool stack_trace_on_ = false;  // FIRE_B200_STACK_TRACE=1: record the per-phase timeline
     size_t stack_trace_words_ = 0;
 };

@@ -237,6 +237,35 @@ __global__ void dequant_w4_bf16_kernel(const uint8_t* __restrict__ qw, const flo
     }
 }
 
+// W in the layer-stack item layout (16 rows x 256 K per 2208-byte item, see layer_stack.h)
+// -> BF16 [N, K] in the items' row order; one thread per 8 weights
+__global__ void dequant_items_bf16_kernel(const uint8_t* __restrict__ items, __nv_bfloat16* __restrict__ out, int N,
+                                          int K) {
+    const long long total = static_cast<long long>(N) * (K / 8);
+    const int ipr = K / 256;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int n = static_cast<int>(i / (K / 8));
+        const int k = static_cast<int>(i % (K / 8)) * 8;
+        const int tile = n >> 4, r = n & 15, it = k >> 8, kl = k & 255;
+        const int gi = kl >> 7, b = (kl & 127) >> 1;  // group in the item, byte in the row's 64-byte group
+        const uint8_t* item = items + (static_cast<size_t>(tile) * ipr + it) * 2208;
+        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(
+            item + (((r >> 3) * 2 + gi) * 32 + (r & 7) * 4 + (b >> 4)) * 16 + (b & 15)));
+        const float s = __ldg(reinterpret_cast<const float*>(item + 2048) + r * 2 + gi);
+        const float z = static_cast<float>(__ldg(item + 2176 + r * 2 + gi));
+        uint32_t packed[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float lo = s * (static_cast<float>((w >> (8 * j)) & 0xF) - z);
+            const float hi = s * (static_cast<float>((w >> (8 * j + 4)) & 0xF) - z);
+            const __nv_bfloat162 bb = __floats2bfloat162_rn(lo, hi);
+            packed[j] = *reinterpret_cast<const uint32_t*>(&bb);
+        }
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(n) * K + k) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+}
+
 // X FP32 -> x_hi = bf16(x), x_lo = bf16(x - x_hi), 8 elements per thread
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
@@ -300,34 +329,62 @@ size_t prefill_workspace_bytes(int M, int N, int K) {
     return 2 * align256(static_cast<size_t>(M) * K * 2) + align256(static_cast<size_t>(N) * K * 2);
 }
 
-cudaError_t prefill_w4_launch(const float* x, const uint8_t* qw, const float* scales, const uint8_t* zeros, float* y,
-                              int M, int N, int K, void* workspace, size_t workspace_bytes, int* err,
-                              cudaStream_t s) {
+size_t prefill_gemm_workspace_bytes(int M, int K) { return 2 * align256(static_cast<size_t>(M) * K * 2); }
+
+cudaError_t prefill_dequant_rows_launch(const uint8_t* qw, const float* scales, const uint8_t* zeros, int N, int K,
+                                        void* w_bf16, cudaStream_t s) {
+    if (N <= 0 || K % 128 || reinterpret_cast<uintptr_t>(w_bf16) % 16 || reinterpret_cast<uintptr_t>(qw) % 4)
+        return cudaErrorInvalidValue;
+    const long long w8 = static_cast<long long>(N) * K / 8;
+    dequant_w4_bf16_kernel<<<static_cast<int>(std::min<long long>((w8 + 255) / 256, 8192)), 256, 0, s>>>(
+        qw, scales, zeros, static_cast<__nv_bfloat16*>(w_bf16), N, K);
+    return cudaGetLastError();
+}
+
+cudaError_t prefill_dequant_items_launch(const uint8_t* items, int N, int K, void* w_bf16, cudaStream_t s) {
+    if (N % 16 || K % 256 || reinterpret_cast<uintptr_t>(w_bf16) % 16 || reinterpret_cast<uintptr_t>(items) % 16)
+        return cudaErrorInvalidValue;
+    const long long w8 = static_cast<long long>(N) * K / 8;
+    dequant_items_bf16_kernel<<<static_cast<int>(std::min<long long>((w8 + 255) / 256, 8192)), 256, 0, s>>>(
+        items, static_cast<__nv_bfloat16*>(w_bf16), N, K);
+    return cudaGetLastError();
+}
+
+cudaError_t prefill_gemm_launch(const float* x, const void* w_bf16, float* y, int M, int N, int K, void* workspace,
+                                size_t workspace_bytes, int* err, cudaStream_t s) {
     if (!prefill_supported(M, N, K, 128) || workspace == nullptr || err == nullptr) return cudaErrorInvalidValue;
-    if (workspace_bytes < prefill_workspace_bytes(M, N, K)) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(workspace)) % 16 ||
-        reinterpret_cast<uintptr_t>(qw) % 4)
+    if (workspace_bytes < prefill_gemm_workspace_bytes(M, K)) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(workspace) |
+         reinterpret_cast<uintptr_t>(w_bf16)) % 16)
         return cudaErrorInvalidValue;
     const size_t xbytes = align256(static_cast<size_t>(M) * K * 2);
     __nv_bfloat16* xb = static_cast<__nv_bfloat16*>(workspace);
     __nv_bfloat16* xl = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + xbytes);
-    __nv_bfloat16* wb = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + 2 * xbytes);
     const long long n8 = static_cast<long long>(M) * K / 8;
     split_bf16_kernel<<<static_cast<int>(std::min<long long>((n8 + 255) / 256, 4096)), 256, 0, s>>>(x, xb, xl, n8);
-    const long long w8 = static_cast<long long>(N) * K / 8;
-    dequant_w4_bf16_kernel<<<static_cast<int>(std::min<long long>((w8 + 255) / 256, 8192)), 256, 0, s>>>(qw, scales, zeros, wb,
-                                                                                                       N, K);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     CUtensorMap ma, malo, mb;
     if (!make_map(&ma, xb, M, K, kPrefillBM) || !make_map(&malo, xl, M, K, kPrefillBM) ||
-        !make_map(&mb, wb, N, K, kPrefillBN))
+        !make_map(&mb, w_bf16, N, K, kPrefillBN))
         return cudaErrorNotSupported;
     e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     dim3 grid(static_cast<unsigned>(N / kPrefillBN), static_cast<unsigned>(M / kPrefillBM));
     prefill_gemm_kernel<<<grid, kThreads, kSmemBytes, s>>>(ma, malo, mb, y, M, N, K, err);
     return cudaGetLastError();
+}
+
+cudaError_t prefill_w4_launch(const float* x, const uint8_t* qw, const float* scales, const uint8_t* zeros, float* y,
+                              int M, int N, int K, void* workspace, size_t workspace_bytes, int* err,
+                              cudaStream_t s) {
+    if (!prefill_supported(M, N, K, 128) || workspace == nullptr || err == nullptr) return cudaErrorInvalidValue;
+    if (workspace_bytes < prefill_workspace_bytes(M, N, K)) return cudaErrorInvalidValue;
+    const size_t gws = prefill_gemm_workspace_bytes(M, K);
+    void* wb = static_cast<char*>(workspace) + gws;
+    cudaError_t e = prefill_dequant_rows_launch(qw, scales, zeros, N, K, wb, s);
+    if (e != cudaSuccess) return e;
+    return prefill_gemm_launch(x, wb, y, M, N, K, workspace, gws, err, s);
 }
 
 }  // namespace fb

@@ -16,6 +16,15 @@ constexpr int kPrefillBK = 64;   // K per pipeline stage (one 128-byte swizzle r
 bool prefill_supported(int M, int N, int K, int group);
 // Scratch: BF16 x_hi and x_lo [M, K] and the dequantised W [N, K].
 size_t prefill_workspace_bytes(int M, int N, int K);
+// The two halves of prefill_w4_launch, for callers that keep their own weight layout:
+// dequantise (.fire rows, or layer-stack items in their row order) into BF16 [N, K], then
+// Y = X . W^T with X split into BF16 hi/lo terms (scratch prefill_gemm_workspace_bytes).
+size_t prefill_gemm_workspace_bytes(int M, int K);
+cudaError_t prefill_dequant_rows_launch(const uint8_t* qw, const float* scales, const uint8_t* zeros, int N, int K,
+                                        void* w_bf16, cudaStream_t s);
+cudaError_t prefill_dequant_items_launch(const uint8_t* items, int N, int K, void* w_bf16, cudaStream_t s);
+cudaError_t prefill_gemm_launch(const float* x, const void* w_bf16, float* y, int M, int N, int K, void* workspace,
+                                size_t workspace_bytes, int* err, cudaStream_t s);
 cudaError_t prefill_w4_launch(const float* x, const uint8_t* qw, const float* scales, const uint8_t* zeros, float* y,
                               int M, int N, int K, void* workspace, size_t workspace_bytes, int* err,
                               cudaStream_t s);

@@ -138,6 +138,14 @@ class Qwen3Engine:
     def kernels_per_step(self) -> int:
         return self._L.fire_b200_qwen3_kernels_per_step(self._h)
 
+    def prefill(self, tokens: Sequence[int], logits=None, stream=None) -> None:
+        """Consume the prompt tokens at positions length.. in one batched pass (see
+        fire_b200_qwen3_prefill); logits of the last token into `logits` if given."""
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        ptr = logits.data_ptr() if logits is not None else None
+        N.check(self._L.fire_b200_qwen3_prefill(self._h, ids.ctypes.data, len(ids), ptr, N.stream_handle(stream)),
+                "prefill")
+
     def time_layer_stack(self, reps: int = 5, stream=None) -> float:
         """Average device milliseconds of one launch of the layer-stack kernel alone."""
         ms = C.c_float(0.0)

@@ -89,6 +89,16 @@ const float* fire_b200_qwen3_logits(const fire_b200_qwen3* m);
 /* Kernels of this library one sampled decode step launches (CUDA graph nodes). */
 int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m);
 
+/* Batched prefill (the reference prefills token by token, demo/qwen_chat.cpp:202-213):
+ * consume n prompt ids (host memory) at positions length()..length()+n-1 and leave the KV
+ * cache, the length and the last token's logits (engine buffer, and logits_out if not
+ * NULL) as n calls of fire_b200_qwen3_forward would. On one GPU, with 64 or more tokens,
+ * the projections run on the tensor cores in chunks of 512 rows (BF16 weights, x as two BF16
+ * terms, FP32 accumulation), so the values match forward() to about 1e-3; otherwise it is
+ * forward() per token. Synchronises with `stream` before returning. */
+int fire_b200_qwen3_prefill(fire_b200_qwen3* m, const int32_t* tokens, int n, float* logits_out,
+                            void* stream);
+
 /* Diagnostics (no reference counterpart): with FIRE_B200_STACK_TRACE=1 in the
  * environment at create time, the persistent layer-stack kernel records a per-phase
  * timeline of its last launch, [CTAs][layers][5 phases][13 values]: 5 stamps of the
