@@ -23,7 +23,8 @@
 //
 // Synchronisation. Ring slots have "full" (TMA transaction count) and "empty" (one
 // consumer-warp arrival) mbarriers. Phases wait on per-(layer, phase) counters that
-// each CTA bumps once, after a __threadfence(), when its units of that phase are done.
+// each CTA bumps once (a release reduction after a consumer barrier) when its units of
+// that phase are done; readers take the counter with an acquire load.
 // Every wait is bounded: on timeout the kernel records kStackErrTimeout in the decode
 // state, stops issuing copies, keeps the barrier structure of its consumer warps
 // intact (work is skipped, barriers are still met), waits for its copies in flight and
@@ -446,9 +447,10 @@ __device__ void wait_phase(const StackArgs& a, const Shared& sh, int l, int p, u
     }
     cbar();
 }
+// one thread publishes the phase after a consumer barrier: a release reduction orders
+// every store the CTA made before the barrier ahead of the counter update
 __device__ __forceinline__ void signal_phase(const StackArgs& a, int l, int p) {
-    __threadfence();
-    atomicAdd(a.sync + l * kStackPhases + p, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + l * kStackPhases + p) : "memory");
 }
 
 __device__ float csum(float v, float* red) {
@@ -570,23 +572,42 @@ __device__ __forceinline__ ItemRegs load_item(const uint8_t* item) {
 // share of rows gq (acc0) and gq + 8 (acc1); the quad's four lanes are added later.
 // Lane c of a quad holds digit columns 2c, 2c+1 of the MMA result: c = 0 digits 0/1,
 // c = 1 digits 2/3 (weight 128^2), c >= 2 the unused zero columns.
-__device__ __forceinline__ void item_accumulate(const ItemRegs& it, const Shared& sh, int groups, int g0, float& acc0,
-                                                float& acc1) {
+// The B operand (x digits) and the float2 {sum, 2^-e} of the two 128-groups of an item.
+struct Digits {
+    uint4 b[2][2];  // [group][2 x 16 bytes]: digit column gq (lanes gq < 4), quad c
+    float2 gx[2];
+};
+
+__device__ __forceinline__ Digits load_digits(const Shared& sh, int groups, int g0) {
     const int lane = threadIdx.x & 31, gq = lane >> 2, c = lane & 3;
-    const auto& wv = it.wv;
-    const uint8_t* xd = sh.x;
     const float2* xg = reinterpret_cast<const float2*>(sh.x + static_cast<size_t>(groups) * 512);
+    Digits d;
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+        d.b[gi][0] = d.b[gi][1] = make_uint4(0, 0, 0, 0);
+        if (gq < 4) {
+            const uint4* src =
+                reinterpret_cast<const uint4*>(sh.x + ((static_cast<size_t>(g0 + gi) * 4 + gq) * 4 + c) * 32);
+            d.b[gi][0] = src[0];
+            d.b[gi][1] = src[1];
+        }
+        d.gx[gi] = xg[g0 + gi];
+    }
+    return d;
+}
+
+// Accumulate one item (16 rows x 256 K) against its groups' digits into this lane's
+// share of rows gq (acc0) and gq + 8 (acc1); the quad's four lanes are added later.
+// Lane c of a quad holds digit columns 2c, 2c+1 of the MMA result: c = 0 digits 0/1,
+// c = 1 digits 2/3 (weight 128^2), c >= 2 the unused zero columns.
+__device__ __forceinline__ void item_accumulate(const ItemRegs& it, const Digits& dg, float& acc0, float& acc1) {
+    const int lane = threadIdx.x & 31, c = lane & 3;
+    const auto& wv = it.wv;
     const float cw = c == 0 ? 1.0f : 16384.0f;
     const float zmul = c == 0 ? -1.0f : 0.0f;
 #pragma unroll
     for (int gi = 0; gi < 2; ++gi) {
-        const int g = g0 + gi;
-        uint4 b4[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-        if (gq < 4) {
-            const uint4* src = reinterpret_cast<const uint4*>(xd + ((static_cast<size_t>(g) * 4 + gq) * 4 + c) * 32);
-            b4[0] = src[0];
-            b4[1] = src[1];
-        }
+        const uint4* b4 = dg.b[gi];
         const uint32_t wg[4] = {wv[0][gi].x, wv[0][gi].y, wv[0][gi].z, wv[0][gi].w};
         const uint32_t wh[4] = {wv[1][gi].x, wv[1][gi].y, wv[1][gi].z, wv[1][gi].w};
         int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
@@ -598,7 +619,7 @@ __device__ __forceinline__ void item_accumulate(const ItemRegs& it, const Shared
         // d_even + 128 d_odd: exact in int32 (|column sum| <= 128 * 15 * 127), one rounding to float
         const int t0 = (da[0] + db[0]) + 128 * (da[1] + db[1]);
         const int t1 = (da[2] + db[2]) + 128 * (da[3] + db[3]);
-        const float2 gx = xg[g];
+        const float2 gx = dg.gx[gi];
         // zero point as float: 2^23 + z, minus 2^23
         const float zf0 = __uint_as_float(__byte_perm(it.z0, 0x4B000000u, 0x7540 + gi)) - 8388608.0f;
         const float zf1 = __uint_as_float(__byte_perm(it.z1, 0x4B000000u, 0x7540 + gi)) - 8388608.0f;
@@ -646,8 +667,14 @@ __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& s
     float v = 0.0f;
     if (lane < 16) {
         const float* pp = sh.part + static_cast<size_t>(k) * ph.ipu * 16 + lane;
-        for (int j = 0; j < ph.ipu; ++j) v += pp[j * 16];
-        v *= scale;
+        float v4[4] = {0.f, 0.f, 0.f, 0.f};  // four chains, combined in a fixed order
+        int j = 0;
+        for (; j + 4 <= ph.ipu; j += 4) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v4[q] += pp[(j + q) * 16];
+        }
+        for (; j < ph.ipu; ++j) v4[0] += pp[j * 16];
+        v = ((v4[0] + v4[1]) + (v4[2] + v4[3])) * scale;
     }
     if (ph.kparts == 1) {
         tile_epilogue(a, p, tile, v, res);
@@ -688,12 +715,18 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
     int k = warp / ph.ipu, j = warp % ph.ipu;
     Slot sl = slot_of(seq_base + static_cast<unsigned>(warp), S);
     int kp = ph.kparts == 1 ? 0 : (first + k * sc.grid) % ph.kparts;
+    // with one K part and W items per unit, every item of this warp uses the same two
+    // groups: their digits stay in registers for the phase
+    const bool fixed = ph.kparts == 1 && ph.ipu == W;
+    Digits dg{};
+    if (fixed && warp < total) dg = load_digits(sh, groups, 2 * j);
     for (int s = warp; s < total; s += W) {
         if (wait_item(a, sh, sl, waited)) {
             const ItemRegs it = load_item(sh.ring + static_cast<size_t>(sl.index) * kItemBytes);
             release_item(sh, sl);
+            if (!fixed) dg = load_digits(sh, groups, 2 * (kp * ph.ipu + j));
             float acc0 = 0.0f, acc1 = 0.0f;
-            item_accumulate(it, sh, groups, 2 * (kp * ph.ipu + j), acc0, acc1);
+            item_accumulate(it, dg, acc0, acc1);
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
             acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
             acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
