@@ -414,7 +414,7 @@ def run_ours(args):
     barrier()
     ms_e2e = max(h0.elapsed_time(h1), wall_e2e * 1e3)
     # roofline of the dominant kernel, measured live
-    if eng.kernels_per_step == 4:  # persistent layer-stack kernel
+    if eng.kernels_per_step <= 5:  # persistent layer-stack kernel (+ the TP rank select)
         pos = eng.length
         kern_name = "stack_kernel"
         kern_bytes = layer_stack_bytes(p, world, pos)

@@ -68,7 +68,49 @@ Qwen3Engine::~Qwen3Engine() {
     if (graph_step_) cudaGraphExecDestroy(graph_step_);
     if (host_state_) cudaFreeHost(host_state_);
     if (host_token_) cudaFreeHost(host_token_);
+    for (int r = 0; r < kStackMaxTp; ++r)
+        if (xchg_peer_[r] && xchg_peer_[r] != xchg_) cudaIpcCloseMemHandle(xchg_peer_[r]);
+    if (xchg_) cudaFree(xchg_);
     if (comm_ && nccl().ok) nccl().CommDestroy(comm_);
+}
+
+// Tensor parallel with the layer stack: allocate this rank's exchange block, share its
+// IPC handle with every rank over NCCL (all-gather of the 64-byte handles) and map the
+// peers' blocks. The kernel stores partial sums and bumps counters in those mappings
+// (NVLink peer memory).
+int Qwen3Engine::setup_exchange(std::string* err) {
+    auto fail = [&](int code, const std::string& m) {
+        if (err) *err = m;
+        return code;
+    };
+    const size_t bytes = stack_exchange_bytes(tp_, d_.hidden, d_.layers);
+    FB_CK(cudaMalloc(&xchg_, bytes));
+    FB_CK(cudaMemset(xchg_, 0, bytes));
+    cudaIpcMemHandle_t mine;
+    FB_CK(cudaIpcGetMemHandle(&mine, xchg_));
+    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    void* dh = nullptr;
+    FB_CK(cudaMalloc(&dh, kH * tp_));
+    std::vector<cudaIpcMemHandle_t> all(tp_);
+    cudaStream_t s;
+    int rc = static_cast<int>(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    if (!rc) rc = static_cast<int>(cudaMemcpyAsync(static_cast<char*>(dh) + kH * rank_, &mine, kH, cudaMemcpyHostToDevice, s));
+    if (!rc && nccl().AllGather(static_cast<char*>(dh) + kH * rank_, dh, kH, kNcclUint8, comm_, s) != 0)
+        rc = FIRE_B200_ERR_STATE;
+    if (!rc) rc = static_cast<int>(cudaMemcpyAsync(all.data(), dh, kH * tp_, cudaMemcpyDeviceToHost, s));
+    if (!rc) rc = static_cast<int>(cudaStreamSynchronize(s));
+    cudaStreamDestroy(s);
+    cudaFree(dh);
+    if (rc) return fail(rc, "exchange handle all-gather failed");
+    for (int r = 0; r < tp_; ++r) {
+        if (r == rank_) {
+            xchg_peer_[r] = xchg_;
+            continue;
+        }
+        const cudaError_t e = cudaIpcOpenMemHandle(&xchg_peer_[r], all[r], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return fail(static_cast<int>(e), std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+    }
+    return 0;
 }
 
 int Qwen3Engine::create(const Qwen3Dims& d, const std::vector<TensorSrc>& tensors, const EngineOptions& opt,
@@ -104,25 +146,33 @@ int Qwen3Engine::create(const Qwen3Dims& d, const std::vector<TensorSrc>& tensor
     e->f_ = d.inter / t;
     e->v_ = d.vocab / t;
     e->v_off_ = e->rank_ * e->v_;
-    // the persistent layer-stack kernel serves tensor-parallel size 1 when the shapes fit
-    // (FIRE_B200_LAYER_STACK=0 selects the per-op kernels)
-    if (t == 1) {
+    if (t > 1) {
+        const int nr = nccl_comm_init_rank(&e->comm_, t, opt.nccl_id, e->rank_);
+        if (nr != 0) return fail(FIRE_B200_ERR_STATE, std::string("ncclCommInitRank: ") + nccl().GetErrorString(nr));
+    }
+    // the persistent layer-stack kernel serves the step when the shapes fit
+    // (FIRE_B200_LAYER_STACK=0 selects the per-op kernels); under tensor parallelism (up to
+    // kStackMaxTp ranks) when FIRE_B200_TP_STACK=1. Every rank reaches the same decision:
+    // it depends only on the shapes and the environment the launcher gives all ranks.
+    {
         const char* env = std::getenv("FIRE_B200_LAYER_STACK");
-        if (env == nullptr || std::strcmp(env, "0") != 0) {
+        const char* tp_env = std::getenv("FIRE_B200_TP_STACK");
+        const bool tp_ok = t == 1 || (t <= kStackMaxTp && tp_env != nullptr && std::strcmp(tp_env, "1") == 0);
+        if ((env == nullptr || std::strcmp(env, "0") != 0) && tp_ok) {
             StackArgs probe = e->stack_template(d.max_seq);
             e->stack_ = stack_plan(&probe, e->sms_);
             const char* tr = std::getenv("FIRE_B200_STACK_TRACE");
             e->stack_trace_on_ = e->stack_ && tr != nullptr && std::strcmp(tr, "1") == 0;
+        }
+        if (e->stack_ && t > 1) {
+            const int xr = e->setup_exchange(err);
+            if (xr != 0) return xr;
         }
     }
     e->weight_arena_.reset(new DeviceArena(e->device_));
     e->runtime_arena_.reset(new DeviceArena(e->device_));
     const int rc = e->import_weights(tensors, err);
     if (rc != 0) return rc;
-    if (t > 1) {
-        const int nr = nccl_comm_init_rank(&e->comm_, t, opt.nccl_id, e->rank_);
-        if (nr != 0) return fail(FIRE_B200_ERR_STATE, std::string("ncclCommInitRank: ") + nccl().GetErrorString(nr));
-    }
     *out = std::move(e);
     return 0;
 }
@@ -419,6 +469,7 @@ int Qwen3Engine::prepare(int capacity) {
         sa.rope_sin = rope_sin_;
         sa.rope_cos = rope_cos_;
         sa.sync = stack_sync_;
+        if (tp_ > 1) stack_bind_exchange(&sa, tp_, rank_, xchg_peer_);
         sa.trace = nullptr;
         if (stack_trace_words_) {
             sa.trace = static_cast<unsigned long long*>(A(stack_trace_words_ * 8));
@@ -597,10 +648,13 @@ int Qwen3Engine::enqueue_step(cudaStream_t s, bool sample) {
             FB_RC(allreduce(down_part_));
         }
     }
-    // final norm + LM head (qwen.cpp:294-301)
-    const float* hx = tp_ > 1 ? attn_res_ : hidden_;
-    const float* hadd = tp_ > 1 ? down_part_ : nullptr;
-    float* hsum = tp_ > 1 ? hidden_ : nullptr;
+    // final norm + LM head (qwen.cpp:294-301); the layer stack leaves the reduced
+    // residual stream in hidden_ at every TP size, the per-op path leaves its last
+    // all-reduced down partial to add here
+    const bool add_down = tp_ > 1 && !stack_;
+    const float* hx = add_down ? attn_res_ : hidden_;
+    const float* hadd = add_down ? down_part_ : nullptr;
+    float* hsum = add_down ? hidden_ : nullptr;
     if (head_kind_ == 2) {
         W4Args h{};
         h.x = hx;
@@ -652,7 +706,7 @@ int Qwen3Engine::launch_step(cudaStream_t s, bool sample) {
 }
 
 int Qwen3Engine::kernels_per_step() const {
-    if (stack_) return 4;  // embedding, layer stack, LM head, argmax
+    if (stack_) return 4 + (tp_ > 1 ? 1 : 0);  // embedding, layer stack, LM head, argmax (+ rank select)
     return 5 * d_.layers + 3 + (tp_ > 1 ? 1 : 0);
 }
 

@@ -165,8 +165,13 @@ class Qwen3Engine {
     cudaGraphExec_t graph_fwd_ = nullptr, graph_step_ = nullptr;
     NcclComm comm_ = nullptr;
 
-    // persistent layer-stack kernel (tensor-parallel size 1): weights in item layout
+    // persistent layer-stack kernel: weights in item layout
     bool stack_ = false;
+    // tensor parallel with the layer stack: this rank's exchange block (cudaMalloc, so it
+    // can be shared by IPC handle) and every rank's block as mapped here (own at [rank])
+    void* xchg_ = nullptr;
+    void* xchg_peer_[kStackMaxTp] = {};
+    int setup_exchange(std::string* err);
     bool stack_coop_ = true;  // cooperative launch (falls back if the runtime refuses it)
     StackLayer* stack_layers_ = nullptr;  // device [layers]
     StackArgs stack_args_{};

@@ -79,21 +79,19 @@ __device__ __forceinline__ void rope_rotate(float& a, float& b, float fcr, float
 }
 
 // One 128-wide head held by a warp, lane l owning dims 4l..4l+3: per-head RMSNorm with
-// weight nw (rmsnorm_kernel.cpp:41-67) then half-split RoPE at the cache rows sin_row /
-// cos_row [64] (rope_kernel.cpp:26-52); the RoPE partner of lane l is lane l^16.
-__device__ __forceinline__ void head_norm_rope(float (&v)[4], const float* nw, const float* sin_row,
-                                               const float* cos_row, float eps) {
+// weights w4 = nw[4l..4l+3] (rmsnorm_kernel.cpp:41-67) then half-split RoPE with
+// s4 / c4 = sin_row / cos_row [4(l & 15)..+3] of this position (rope_kernel.cpp:26-52);
+// the RoPE partner of lane l is lane l^16. The weights and rows come in as arguments
+// so a caller can load them early.
+__device__ __forceinline__ void head_norm_rope_loaded(float (&v)[4], float4 w4, float4 s4, float4 c4, float eps) {
     const int lane = threadIdx.x & 31;
     float ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], v[3] * v[3])));
     ss = warp_sum(ss);
     const float scale = 1.0f / sqrtf(ss / 128.0f + eps);
-    const float4 w4 = reinterpret_cast<const float4*>(nw)[lane];
     v[0] = v[0] * w4.x * scale;
     v[1] = v[1] * w4.y * scale;
     v[2] = v[2] * w4.z * scale;
     v[3] = v[3] * w4.w * scale;
-    const float4 s4 = reinterpret_cast<const float4*>(sin_row)[lane & 15];
-    const float4 c4 = reinterpret_cast<const float4*>(cos_row)[lane & 15];
     const float sn[4] = {s4.x, s4.y, s4.z, s4.w}, cs[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -103,6 +101,13 @@ __device__ __forceinline__ void head_norm_rope(float (&v)[4], const float* nw, c
         rope_rotate(a0, b0, cs[j], sn[j]);
         v[j] = lane < 16 ? a0 : b0;
     }
+}
+
+__device__ __forceinline__ void head_norm_rope(float (&v)[4], const float* nw, const float* sin_row,
+                                               const float* cos_row, float eps) {
+    const int lane = threadIdx.x & 31;
+    head_norm_rope_loaded(v, reinterpret_cast<const float4*>(nw)[lane], reinterpret_cast<const float4*>(sin_row)[lane & 15],
+                          reinterpret_cast<const float4*>(cos_row)[lane & 15], eps);
 }
 
 }  // namespace fb

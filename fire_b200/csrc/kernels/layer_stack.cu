@@ -76,6 +76,11 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned long long gtime() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -453,6 +458,38 @@ __device__ __forceinline__ void signal_phase(const StackArgs& a, int l, int p) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + l * kStackPhases + p) : "memory");
 }
 
+// Tensor parallel: this CTA's partial rows of (l, p) are stored in every rank's block.
+// A local ticket (acquire-release at system scope, after the block barrier) finds the
+// rank's last CTA, which then bumps every rank's exchange counter with a system-scope
+// release; the chain orders every CTA's remote stores before each rank sees its count.
+__device__ __forceinline__ void signal_exchange(const StackArgs& a, int l, int p, unsigned ctas) {
+    unsigned old;
+    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + l * kStackPhases + p) : "memory");
+    if (old == ctas - 1)
+        for (int r = 0; r < a.tp; ++r)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xctr[r] + 2 * l + (p == 4 ? 1 : 0)) : "memory");
+}
+// thread 0 waits until every rank finished (l, o) or (l, down) in this launch; then all
+// consumers sync
+__device__ void wait_exchange(const StackArgs& a, const Shared& sh, int l, int which, unsigned target) {
+    if (threadIdx.x == 0 && !failed(sh)) {
+        const unsigned* ctr = a.xctr[a.rank] + 2 * l + which;
+        bool ok = false;
+        const unsigned long long t0 = gtime();
+        for (int i = 0; i < kSpinLimit; ++i) {
+            if (ld_acquire_sys(ctr) >= target) { ok = true; break; }
+            if ((i & 63) == 63 && state_failed(a.state)) break;
+            if (overdue(i, t0)) break;
+            __nanosleep(32);
+        }
+        if (!ok) {
+            if (!state_failed(a.state)) record_timeout(a.state);
+            mark_failed(sh);
+        }
+    }
+    cbar();
+}
+
 __device__ float csum(float v, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     v = warp_sum(v);
@@ -507,7 +544,12 @@ __device__ __forceinline__ void store_digits(const float (&v)[4], int g, const S
     }
 }
 
-__device__ void stage_x(const float* x, const float* norm_w, const StackPhase& ph, bool own, const Shared& sh) {
+// Tensor parallel (parts != nullptr): the input is x + (p_0 + p_1 + ... ) over the ranks'
+// partials `parts` [tp][k] (this rank's exchange block), the same sum on every rank; of
+// the `writers` CTAs taking part in the phase, the one of rank `writer` = g mod writers
+// also stores group g of the sum to `keep`.
+__device__ void stage_x(const float* x, const float* norm_w, const StackPhase& ph, bool own, const Shared& sh,
+                        const float* parts, int tp, float* keep, int writer, int writers) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int groups = ph.k >> 7;
     const int mine = own ? 2 * ph.kparts : (groups - warp + W - 1) / W;  // groups this warp stages
@@ -521,6 +563,24 @@ __device__ void stage_x(const float* x, const float* norm_w, const StackPhase& p
 #pragma unroll
         for (int i = 0; i < kStageRegs; ++i)
             v[i] = b0 + i < mine ? __ldcg(x4 + group_of(b0 + i) * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (parts != nullptr) {
+            const float4* p4 = reinterpret_cast<const float4*>(parts);
+            const int k4 = ph.k >> 2;
+#pragma unroll
+            for (int i = 0; i < kStageRegs; ++i) {
+                if (b0 + i < mine) {
+                    const int idx = group_of(b0 + i) * 32 + lane;
+                    float4 sum = __ldcg(p4 + idx);
+                    for (int r = 1; r < tp; ++r) {
+                        const float4 t = __ldcg(p4 + static_cast<size_t>(r) * k4 + idx);
+                        sum = make_float4(sum.x + t.x, sum.y + t.y, sum.z + t.z, sum.w + t.w);
+                    }
+                    v[i] = make_float4(v[i].x + sum.x, v[i].y + sum.y, v[i].z + sum.z, v[i].w + sum.w);
+                    if (group_of(b0 + i) % writers == writer)
+                        reinterpret_cast<float4*>(keep)[idx] = v[i];
+                }
+            }
+        }
         if (norm_w != nullptr) {
 #pragma unroll
             for (int i = 0; i < kStageRegs; ++i) {
@@ -633,10 +693,13 @@ __device__ __forceinline__ void item_accumulate(const ItemRegs& it, const Digits
 // Epilogue of one finished row tile; lane r < 16 holds the full sum of row tile*16 + r.
 // The residual input of a phase's rows (hidden for o, attn_res for down); it is final
 // before the phase starts, so it is read ahead of the epilogue.
+template <bool kTp>
 __device__ __forceinline__ const float* phase_residual(const StackArgs& a, int p) {
+    if (kTp) return nullptr;  // added to the reduced sums when the next phase stages them
     return p == 2 ? a.hidden_buf : (p == 4 ? a.attn_res : nullptr);
 }
 
+template <bool kTp>
 __device__ __forceinline__ void tile_epilogue(const StackArgs& a, int p, int tile, float v, float res) {
     const int lane = threadIdx.x & 31;
     const float up = __shfl_down_sync(0xffffffffu, v, 8);
@@ -645,12 +708,18 @@ __device__ __forceinline__ void tile_epilogue(const StackArgs& a, int p, int til
     if (p == 0) {
         a.qkv[row] = v;
     } else if (p == 2) {
-        a.attn_res[row] = res + v;  // residual (qwen.cpp:262)
+        if (kTp) {  // row-parallel partial sums to every rank (the residual is added when staging)
+            for (int r = 0; r < a.tp; ++r) a.xo[r][static_cast<size_t>(a.rank) * a.hidden + row] = v;
+        } else {
+            a.attn_res[row] = res + v;  // residual (qwen.cpp:262)
+        }
     } else if (p == 3) {
         if (lane < 8) {
             const float silu = v * 1.0f / (1.0f + expf(-v));  // swiglu_kernel.cu:11-12
             a.act[tile * 8 + lane] = silu * up;
         }
+    } else if (kTp) {
+        for (int r = 0; r < a.tp; ++r) a.xdown[r][static_cast<size_t>(a.rank) * a.hidden + row] = v;
     } else {
         a.hidden_buf[row] = res + v;  // residual (qwen.cpp:291)
     }
@@ -658,6 +727,7 @@ __device__ __forceinline__ void tile_epilogue(const StackArgs& a, int p, int til
 
 // Finish unit k of this CTA's units in phase p (one warp): add its item partial sums in
 // item order and apply the epilogue; split-K partials meet through a per-tile ticket.
+template <bool kTp>
 __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& sc, int p, int first, int k,
                             float scale, float res) {
     const int lane = threadIdx.x & 31;
@@ -677,7 +747,7 @@ __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& s
         v = ((v4[0] + v4[1]) + (v4[2] + v4[3])) * scale;
     }
     if (ph.kparts == 1) {
-        tile_epilogue(a, p, tile, v, res);
+        tile_epilogue<kTp>(a, p, tile, v, res);
     } else {
         if (lane < 16) a.kpart[static_cast<size_t>(kp) * ph.n + tile * 16 + lane] = v;
         __threadfence();
@@ -691,12 +761,13 @@ __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& s
             v = 0.0f;
             if (lane < 16)
                 for (int q = 0; q < ph.kparts; ++q) v += __ldcg(a.kpart + static_cast<size_t>(q) * ph.n + tile * 16 + lane);
-            tile_epilogue(a, p, tile, v, res);
+            tile_epilogue<kTp>(a, p, tile, v, res);
             if (lane == 0) *ticket = 0u;
         }
     }
 }
 
+template <bool kTp>
 __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc, int l, int p, int first, int count,
                            unsigned seq_base) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -705,7 +776,7 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
     const int total = count * ph.ipu;
     long long waited = 0;
     // residual rows of the unit this warp finishes first (k = warp), read ahead
-    const float* resid = phase_residual(a, p);
+    const float* resid = phase_residual<kTp>(a, p);
     float res0 = 0.0f;
     if (resid != nullptr && warp < count && lane < 16)
         res0 = __ldcg(resid + ((first + warp * sc.grid) / ph.kparts) * 16 + lane);
@@ -770,12 +841,16 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
             float res = res0;
             if (k != warp && resid != nullptr && lane < 16)
                 res = __ldcg(resid + ((first + k * sc.grid) / ph.kparts) * 16 + lane);
-            finish_unit(a, sh, sc, p, first, k, scale, res);
+            finish_unit<kTp>(a, sh, sc, p, first, k, scale, res);
         }
     }
     cbar();
     if (threadIdx.x == 0 && !failed(sh)) {
-        signal_phase(a, l, p);
+        if (kTp && (p == 2 || p == 4)) {
+            signal_exchange(a, l, p, static_cast<unsigned>(min(sc.grid, ph.units)));
+        } else {
+            signal_phase(a, l, p);
+        }
         stamp(a, l, p, 3);
         unsigned long long* w = reinterpret_cast<unsigned long long*>(sh.misc + 4);
         record(a, l, p, 5, *w);
@@ -1022,8 +1097,8 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
     mark(9);
 }
 
-template <int G>
-__device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos) {
+template <int G, bool kTp>
+__device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos, unsigned xtarget) {
     const int tid = threadIdx.x;
     unsigned seq = 0;
     for (int l = 0; l < a.L; ++l) {
@@ -1036,7 +1111,10 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
             // input dependency: the phase before (layer 0's input comes from an earlier launch)
             if (l > 0 || p > 0) {
                 const int lp = p == 0 ? l - 1 : l, pp = p == 0 ? kStackPhases - 1 : p - 1;
-                wait_phase(a, sh, lp, pp, static_cast<unsigned>(min(sc.grid, sc.units(a, pp))));
+                if (kTp && (pp == 2 || pp == 4))  // row-parallel o / down: every rank's sums
+                    wait_exchange(a, sh, lp, pp == 4 ? 1 : 0, xtarget);
+                else
+                    wait_phase(a, sh, lp, pp, static_cast<unsigned>(min(sc.grid, sc.units(a, pp))));
             } else {
                 cbar();
             }
@@ -1062,20 +1140,51 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
             if (!failed(sh)) {
                 const float* x = p == 0 ? a.hidden_buf : (p == 2 ? a.attn_out : (p == 3 ? a.attn_res : a.act));
                 const float* nw = p == 0 ? Ly.attn_norm : (p == 3 ? Ly.ffn_norm : nullptr);
-                stage_x(x, nw, ph, own, sh);
+                // tensor parallel: attn_res = hidden + sum(o partials) (qwen.cpp:262) and
+                // hidden = attn_res + sum(down partials) (qwen.cpp:291), formed here
+                const float* parts = nullptr;
+                float* keep = nullptr;
+                if (kTp && p == 3) {
+                    x = a.hidden_buf;
+                    parts = a.xo[a.rank];
+                    keep = a.attn_res;
+                } else if (kTp && p == 0 && l > 0) {
+                    x = a.attn_res;
+                    parts = a.xdown[a.rank];
+                    keep = a.hidden_buf;
+                }
+                stage_x(x, nw, ph, own, sh, parts, a.tp, keep, first, min(sc.grid, ph.units));
             }
             if (own)
                 __syncwarp();
             else
                 cbar();
             if (tid == 0) stamp(a, l, p, 2);
-            gemv_phase(a, sh, sc, l, p, first, count, seq);
+            gemv_phase<kTp>(a, sh, sc, l, p, first, count, seq);
             seq += static_cast<unsigned>(count * ph.ipu);
+        }
+    }
+    if (kTp) {
+        // the final residual stream for the LM head: hidden = attn_res + sum(down partials)
+        // of the last layer, group g by CTA g mod grid (warp w: g = blockIdx + w grid)
+        wait_exchange(a, sh, a.L - 1, 1, xtarget);
+        const int lane = tid & 31, warp = tid >> 5;
+        const int g = static_cast<int>(blockIdx.x) + warp * sc.grid;
+        if (!failed(sh) && g < (a.hidden >> 7)) {
+            const int idx = g * 32 + lane, h4 = a.hidden >> 2;
+            const float4* p4 = reinterpret_cast<const float4*>(a.xdown[a.rank]);
+            float4 sum = __ldcg(p4 + idx);
+            for (int r = 1; r < a.tp; ++r) {
+                const float4 t = __ldcg(p4 + static_cast<size_t>(r) * h4 + idx);
+                sum = make_float4(sum.x + t.x, sum.y + t.y, sum.z + t.z, sum.w + t.w);
+            }
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(a.attn_res) + idx);
+            reinterpret_cast<float4*>(a.hidden_buf)[idx] = make_float4(b.x + sum.x, b.y + sum.y, b.z + sum.z, b.w + sum.w);
         }
     }
 }
 
-template <int G>
+template <int G, bool kTp>
 __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const Shared sh = carve(a, smem);
@@ -1093,14 +1202,22 @@ __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs
     const bool bad = pos < 0 || pos >= a.capacity || state_failed(a.state);
     if (bad && blockIdx.x == 0 && threadIdx.x == 0 && !state_failed(a.state)) a.state->error = 1;
     __syncthreads();
-    if (bad) return;
+    if (bad) {
+        if (kTp && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(a.epoch, 1u);
+        return;
+    }
     const Sched sc = make_sched(a, pos);
+    // tensor parallel: this launch's exchange counters reach (epoch + 1) * tp
+    const unsigned ep = kTp ? *reinterpret_cast<const volatile unsigned*>(a.epoch) : 0u;
     if (warp == W) {
         producer(a, sh, sc, pos);
     } else if (warp == W + 1) {
         prefetcher(a, sh, sc, pos);
     } else {
-        consumer<G>(a, sh, sc, pos);
+        consumer<G, kTp>(a, sh, sc, pos, (ep + 1u) * static_cast<unsigned>(a.tp));
+        // every CTA read the epoch before its first signal, and CTA 0 gets here only after
+        // all ranks finished the last layer
+        if (kTp && blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.epoch) = ep + 1u;
     }
     pdl_launch_dependents();
 }
@@ -1174,6 +1291,23 @@ size_t stack_sync_words(const StackArgs& a) {
     return static_cast<size_t>(a.L) * kStackPhases + a.kv_heads + tiles;
 }
 
+size_t stack_exchange_bytes(int tp, int hidden, int L) {
+    return 2 * static_cast<size_t>(tp) * hidden * 4 + static_cast<size_t>(L) * 2 * 4 + 4;
+}
+
+void stack_bind_exchange(StackArgs* a, int tp, int rank, void* const* base) {
+    a->tp = tp;
+    a->rank = rank;
+    const size_t part = static_cast<size_t>(tp) * a->hidden * 4;
+    for (int r = 0; r < kStackMaxTp; ++r) {
+        uint8_t* b = r < tp ? static_cast<uint8_t*>(base[r]) : nullptr;
+        a->xo[r] = b ? reinterpret_cast<float*>(b) : nullptr;
+        a->xdown[r] = b ? reinterpret_cast<float*>(b + part) : nullptr;
+        a->xctr[r] = b ? reinterpret_cast<unsigned*>(b + 2 * part) : nullptr;
+    }
+    a->epoch = a->xctr[rank] + 2 * a->L;
+}
+
 size_t stack_kpart_floats(const StackArgs& a) {
     size_t m = 0;
     for (int p = 0; p < kStackPhases; ++p)
@@ -1244,11 +1378,11 @@ bool stack_plan(StackArgs* a, int grid) {
 cudaError_t stack_launch(const StackArgs& a, cudaStream_t s, bool cooperative) {
     void (*kern)(const StackArgs) = nullptr;
     switch (a.q_heads / a.kv_heads) {
-    case 1: kern = stack_kernel<1>; break;
-    case 2: kern = stack_kernel<2>; break;
-    case 4: kern = stack_kernel<4>; break;
-    case 5: kern = stack_kernel<5>; break;
-    case 8: kern = stack_kernel<8>; break;
+    case 1: kern = a.tp > 1 ? stack_kernel<1, true> : stack_kernel<1, false>; break;
+    case 2: kern = a.tp > 1 ? stack_kernel<2, true> : stack_kernel<2, false>; break;
+    case 4: kern = a.tp > 1 ? stack_kernel<4, true> : stack_kernel<4, false>; break;
+    case 5: kern = a.tp > 1 ? stack_kernel<5, true> : stack_kernel<5, false>; break;
+    case 8: kern = a.tp > 1 ? stack_kernel<8, true> : stack_kernel<8, false>; break;
     default: return cudaErrorInvalidValue;
     }
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, a.smem_bytes);

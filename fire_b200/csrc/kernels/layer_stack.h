@@ -33,6 +33,7 @@ constexpr int kStackChunk = 128;  // keys per attention unit
 constexpr int kStackMaxGroup = 8;  // q heads per KV head
 constexpr int kStackErrTimeout = 3;  // DecodeState::error when a bounded wait gave up
 constexpr int kStackTraceSlots = 13;
+constexpr int kStackMaxTp = 8;
 
 enum StackPackMode : int { kPackRows = 0, kPackGateUp = 1 };
 
@@ -87,6 +88,20 @@ struct StackArgs {
     float* attn_ml;    // [q_heads][max_chunks][2]
     float* kpart;      // split-K partial sums [kparts][n]
     unsigned* sync;    // phase counters, attention and tile tickets: zero before each launch
+    // Tensor parallel (tp > 1; Fire's new src/model tensor-parallel layer). o and down are
+    // row-parallel: each rank leaves partial row sums that every rank adds up, in rank
+    // order, while staging the next phase's input. Rank r owns an exchange block (layout
+    // in stack_exchange_bytes) mapped into every rank: xo[r] / xdown[r] are its o / down
+    // partials [tp][hidden], xctr[r] its counters [L][2] (o, down), each bumped once per
+    // rank per launch; epoch counts this rank's completed launches, so a wait targets
+    // (epoch + 1) * tp and the counters are never reset. The epilogues store straight
+    // into the peers' blocks; the last CTA of a rank to finish a phase (local ticket)
+    // bumps every rank's counter with a system-scope release.
+    int tp, rank;
+    float* xo[kStackMaxTp];
+    float* xdown[kStackMaxTp];
+    unsigned* xctr[kStackMaxTp];
+    unsigned* epoch;
     // optional timeline [grid][L][kStackPhases][kStackTraceSlots] of %globaltimer stamps:
     // 0 phase entered, 1 input dependency met, 2 input staged, 3 the CTA's last unit
     // done, 4 the producer issued the phase's last item (0 where the CTA had no units);
@@ -107,6 +122,11 @@ struct StackArgs {
 };
 
 size_t stack_sync_words(const StackArgs& a);
+// Exchange block of one rank: o partials [tp][hidden] f32, down partials [tp][hidden]
+// f32, counters [L][2] u32, then the epoch word.
+size_t stack_exchange_bytes(int tp, int hidden, int L);
+// Point a's exchange fields at the blocks `base[r]` (rank r's block as mapped here).
+void stack_bind_exchange(StackArgs* a, int tp, int rank, void* const* base);
 size_t stack_kpart_floats(const StackArgs& a);
 // Fill the phase geometry and the shared-memory plan for `grid` CTAs; false when the
 // shapes are outside what the kernel handles (the per-op kernels then run instead).

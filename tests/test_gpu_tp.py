@@ -5,6 +5,11 @@ o/down, vocab-sharded head, KV heads by rank) and runs the same steps; the all-g
 logits of every rank must match the unsharded oracle (src/model/qwen.cpp:155-303) within
 the model-level bar, the ranks must agree bit for bit, and the device greedy loop must
 produce the oracle's tokens. Skipped when fewer GPUs are visible.
+
+Two shapes: STACK fits the persistent layer-stack kernel at 2 and 4 ranks (o / down
+partial sums exchanged through NVLink peer memory inside the kernel); P at 4 ranks has a
+384-wide FFN shard the stack does not take, so it runs the per-op kernels with NCCL
+all-reduce. The test checks which path ran.
 """
 import os
 
@@ -20,18 +25,21 @@ pytestmark = pytest.mark.gpu
 
 # heads, FFN width and vocab divide by 4; K slices stay group aligned
 P = Qwen3Profile("tp-gpu", 4096, 512, 512, 1536, 2, 8, 4, 128)
+STACK = Qwen3Profile("tp-stack", 4096, 512, 512, 2048, 2, 8, 4, 128)
 PROMPT = [11, 2024, 7, 99, 3000, 5, 17]
 STEPS = 24
 
 
-def _rank(rank, world, nid, w, q):
+def _rank(rank, world, nid, prof, w, q, stacked):
     try:
+        os.environ["FIRE_B200_TP_STACK"] = "1" if stacked else "0"
         torch.cuda.set_device(rank)
         from fire_b200.engine import Qwen3Engine
 
-        eng = Qwen3Engine(P, w, tp_rank=rank, tp_size=world, nccl_id=nid)
+        eng = Qwen3Engine(prof, w, tp_rank=rank, tp_size=world, nccl_id=nid)
+        kps = eng.kernels_per_step
         eng.prepare(64)
-        logits = torch.empty(P.vocab_size, device="cuda")
+        logits = torch.empty(prof.vocab_size, device="cuda")
         got = []
         for i, t in enumerate(PROMPT):
             eng.forward(t, i, logits)
@@ -43,34 +51,37 @@ def _rank(rank, world, nid, w, q):
         toks = eng.generate(PROMPT[-1], STEPS).cpu().tolist()
         torch.cuda.synchronize()
         eng.close()
-        q.put((rank, np.stack(got), toks, None))
+        q.put((rank, np.stack(got), toks, kps, None))
     except Exception as e:  # reported to the parent
-        q.put((rank, None, None, repr(e)))
+        q.put((rank, None, None, None, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_tp_decode_matches_oracle(cuda, world):
+@pytest.mark.parametrize("prof,world,stacked", [(STACK, 2, True), (STACK, 4, True), (P, 4, False)],
+                         ids=["stack-tp2", "stack-tp4", "per-op-tp4"])
+def test_tp_decode_matches_oracle(cuda, prof, world, stacked):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from fire_b200.engine import nccl_unique_id
     from oracle import oracle as O
 
-    w = synth.generate(P, "mixed", seed=11)
+    w = synth.generate(prof, "mixed", seed=11)
     nid = nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, w, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, prof, w, q, stacked)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     for _ in range(world):
-        rank, logits, toks, err = q.get(timeout=600)
+        rank, logits, toks, kps, err = q.get(timeout=600)
         assert err is None, f"rank {rank}: {err}"
         res[rank] = (logits, toks)
+        # the layer stack runs the step in embedding, stack, head, argmax, rank select
+        assert (kps <= 5) == stacked, kps
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    ref = O.Qwen3Oracle(P, w, capacity=64)
+    ref = O.Qwen3Oracle(prof, w, capacity=64)
     want_logits = [ref.forward(t, i) for i, t in enumerate(PROMPT)]
     lg = want_logits[-1]
     want = []
