@@ -81,6 +81,11 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned long long gtime() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -476,8 +481,10 @@ __device__ void wait_exchange(const StackArgs& a, const Shared& sh, int l, int w
         const unsigned* ctr = a.xctr[a.rank] + 2 * l + which;
         bool ok = false;
         const unsigned long long t0 = gtime();
+        // relaxed polls; one acquire load once the count is there (the counter only grows,
+        // so it reads a value >= target written by the releases it must synchronise with)
         for (int i = 0; i < kSpinLimit; ++i) {
-            if (ld_acquire_sys(ctr) >= target) { ok = true; break; }
+            if (ld_relaxed_sys(ctr) >= target && ld_acquire_sys(ctr) >= target) { ok = true; break; }
             if ((i & 63) == 63 && state_failed(a.state)) break;
             if (overdue(i, t0)) break;
             __nanosleep(32);
