@@ -150,14 +150,14 @@ int Qwen3Engine::create(const Qwen3Dims& d, const std::vector<TensorSrc>& tensor
         const int nr = nccl_comm_init_rank(&e->comm_, t, opt.nccl_id, e->rank_);
         if (nr != 0) return fail(FIRE_B200_ERR_STATE, std::string("ncclCommInitRank: ") + nccl().GetErrorString(nr));
     }
-    // the persistent layer-stack kernel serves the step when the shapes fit
-    // (FIRE_B200_LAYER_STACK=0 selects the per-op kernels); under tensor parallelism (up to
-    // kStackMaxTp ranks) when FIRE_B200_TP_STACK=1. Every rank reaches the same decision:
-    // it depends only on the shapes and the environment the launcher gives all ranks.
+    // the persistent layer-stack kernel serves the step when the shapes fit, also under
+    // tensor parallelism up to kStackMaxTp ranks (FIRE_B200_LAYER_STACK=0 selects the per-op
+    // kernels; FIRE_B200_TP_STACK=0 only under tensor parallelism). Every rank reaches the
+    // same decision: it depends only on the shapes and the environment given to all ranks.
     {
         const char* env = std::getenv("FIRE_B200_LAYER_STACK");
         const char* tp_env = std::getenv("FIRE_B200_TP_STACK");
-        const bool tp_ok = t == 1 || (t <= kStackMaxTp && tp_env != nullptr && std::strcmp(tp_env, "1") == 0);
+        const bool tp_ok = t == 1 || (t <= kStackMaxTp && (tp_env == nullptr || std::strcmp(tp_env, "0") != 0));
         if ((env == nullptr || std::strcmp(env, "0") != 0) && tp_ok) {
             StackArgs probe = e->stack_template(d.max_seq);
             e->stack_ = stack_plan(&probe, e->sms_);
@@ -754,6 +754,8 @@ StackArgs Qwen3Engine::stack_template(int capacity) const {
     a.inter = f_;
     a.q_heads = hq_;
     a.kv_heads = hkv_;
+    a.tp = tp_;
+    a.rank = rank_;
     a.eps = d_.eps;
     a.scale = 1.0f / sqrtf(128.0f);
     a.capacity = capacity;

@@ -76,15 +76,15 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// tensor-parallel exchange words: tag << 32 | float bits, one aligned 64-bit access each
+// (single-copy atomic), relaxed at system scope: no fence, the tag is the validity
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, unsigned long long w) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+__device__ __forceinline__ unsigned long long ld_word_sys(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 __device__ __forceinline__ unsigned long long gtime() {
     unsigned long long t;
@@ -127,6 +127,7 @@ struct Shared {
     uint8_t* x;       // digits [groups][4 digits][4 quads][4 mma][8 B], then float2 [groups]
     float* part;      // [units of the phase][ipu][16] per-item row sums
     int* ucnt;        // [max_units]
+    float* xv;        // tensor parallel: the o / down row sums of the CTA's units [max_units][16]
     float* red;       // [32]
     int* misc;        // [0] failed flag, [2] attention "last" flag, [4..5] traced wait cycles (u64)
 };
@@ -139,6 +140,7 @@ __device__ __forceinline__ Shared carve(const StackArgs& a, uint8_t* base) {
     s.x = base + a.off_x;
     s.part = reinterpret_cast<float*>(base + a.off_part);
     s.ucnt = reinterpret_cast<int*>(base + a.off_ucnt);
+    s.xv = reinterpret_cast<float*>(base + a.off_xv);
     s.red = reinterpret_cast<float*>(base + a.off_misc);
     s.misc = reinterpret_cast<int*>(base + a.off_misc + 32 * sizeof(float));
     return s;
@@ -463,38 +465,54 @@ __device__ __forceinline__ void signal_phase(const StackArgs& a, int l, int p) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + l * kStackPhases + p) : "memory");
 }
 
-// Tensor parallel: this CTA's partial rows of (l, p) are stored in every rank's block.
-// A local ticket (acquire-release at system scope, after the block barrier) finds the
-// rank's last CTA, which then bumps every rank's exchange counter with a system-scope
-// release; the chain orders every CTA's remote stores before each rank sees its count.
-__device__ __forceinline__ void signal_exchange(const StackArgs& a, int l, int p, unsigned ctas) {
-    unsigned old;
-    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + l * kStackPhases + p) : "memory");
-    if (old == ctas - 1)
-        for (int r = 0; r < a.tp; ++r)
-            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.xctr[r] + 2 * l + (p == 4 ? 1 : 0)) : "memory");
-}
-// thread 0 waits until every rank finished (l, o) or (l, down) in this launch; then all
-// consumers sync
-__device__ void wait_exchange(const StackArgs& a, const Shared& sh, int l, int which, unsigned target) {
-    if (threadIdx.x == 0 && !failed(sh)) {
-        const unsigned* ctr = a.xctr[a.rank] + 2 * l + which;
-        bool ok = false;
-        const unsigned long long t0 = gtime();
-        // relaxed polls; one acquire load once the count is there (the counter only grows,
-        // so it reads a value >= target written by the releases it must synchronise with)
-        for (int i = 0; i < kSpinLimit; ++i) {
-            if (ld_relaxed_sys(ctr) >= target && ld_acquire_sys(ctr) >= target) { ok = true; break; }
-            if ((i & 63) == 63 && state_failed(a.state)) break;
-            if (overdue(i, t0)) break;
-            __nanosleep(32);
-        }
-        if (!ok) {
+// Tensor parallel: the value of an exchange word of layer l (see StackArgs); a wait that
+// runs out marks the kernel failed and yields 0
+__device__ __forceinline__ unsigned xtag(unsigned tag_base, int l) { return tag_base + static_cast<unsigned>(l) + 1u; }
+__device__ float word_wait(const StackArgs& a, const Shared& sh, const unsigned long long* p, unsigned tag) {
+    unsigned long long w = ld_word_sys(p);
+    if (static_cast<unsigned>(w >> 32) == tag) return __uint_as_float(static_cast<unsigned>(w));
+    const unsigned long long t0 = gtime();
+    for (int i = 0; i < kSpinLimit; ++i) {
+        w = ld_word_sys(p);
+        if (static_cast<unsigned>(w >> 32) == tag) return __uint_as_float(static_cast<unsigned>(w));
+        if ((i & 63) == 63 && (failed(sh) || state_failed(a.state))) break;
+        if (overdue(i, t0)) {
             if (!state_failed(a.state)) record_timeout(a.state);
-            mark_failed(sh);
+            break;
         }
     }
-    cbar();
+    mark_failed(sh);
+    return 0.0f;
+}
+// (p_0 + p_1 + ... + p_{tp-1}) of elements e0..e0+3 from this rank's exchange words `ll`
+// [tp][n], added in rank order. The words of kWordRanks ranks are loaded together (one
+// round trip per kWordRanks ranks, not one per word); a word still holding an older tag
+// is then polled alone.
+constexpr int kWordRanks = 2;
+__device__ float4 word_sum4(const StackArgs& a, const Shared& sh, const unsigned long long* ll, int n, int e0,
+                            unsigned tag) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r0 = 0; r0 < a.tp; r0 += kWordRanks) {
+        const int nr = min(kWordRanks, a.tp - r0);
+        unsigned long long w[kWordRanks][4];
+#pragma unroll
+        for (int j = 0; j < kWordRanks; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                w[j][c] = j < nr ? ld_word_sys(ll + static_cast<size_t>(r0 + j) * n + e0 + c) : 0ull;
+#pragma unroll
+        for (int j = 0; j < kWordRanks; ++j) {
+            if (j >= nr) break;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float v = static_cast<unsigned>(w[j][c] >> 32) == tag
+                                    ? __uint_as_float(static_cast<unsigned>(w[j][c]))
+                                    : word_wait(a, sh, ll + static_cast<size_t>(r0 + j) * n + e0 + c, tag);
+                s[c] = r0 + j == 0 ? v : s[c] + v;
+            }
+        }
+    }
+    return make_float4(s[0], s[1], s[2], s[3]);
 }
 
 __device__ float csum(float v, float* red) {
@@ -552,11 +570,13 @@ __device__ __forceinline__ void store_digits(const float (&v)[4], int g, const S
 }
 
 // Tensor parallel (parts != nullptr): the input is x + (p_0 + p_1 + ... ) over the ranks'
-// partials `parts` [tp][k] (this rank's exchange block), the same sum on every rank; of
+// partials `parts` [tp][k] (this rank's exchange words, waited for by tag), the same sum on
+// every rank; of
 // the `writers` CTAs taking part in the phase, the one of rank `writer` = g mod writers
 // also stores group g of the sum to `keep`.
-__device__ void stage_x(const float* x, const float* norm_w, const StackPhase& ph, bool own, const Shared& sh,
-                        const float* parts, int tp, float* keep, int writer, int writers) {
+__device__ void stage_x(const StackArgs& a, const float* x, const float* norm_w, const StackPhase& ph, bool own,
+                        const Shared& sh, const unsigned long long* parts, unsigned tag, float* keep, int writer,
+                        int writers) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int groups = ph.k >> 7;
     const int mine = own ? 2 * ph.kparts : (groups - warp + W - 1) / W;  // groups this warp stages
@@ -571,20 +591,13 @@ __device__ void stage_x(const float* x, const float* norm_w, const StackPhase& p
         for (int i = 0; i < kStageRegs; ++i)
             v[i] = b0 + i < mine ? __ldcg(x4 + group_of(b0 + i) * 32 + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (parts != nullptr) {
-            const float4* p4 = reinterpret_cast<const float4*>(parts);
-            const int k4 = ph.k >> 2;
 #pragma unroll
             for (int i = 0; i < kStageRegs; ++i) {
                 if (b0 + i < mine) {
                     const int idx = group_of(b0 + i) * 32 + lane;
-                    float4 sum = __ldcg(p4 + idx);
-                    for (int r = 1; r < tp; ++r) {
-                        const float4 t = __ldcg(p4 + static_cast<size_t>(r) * k4 + idx);
-                        sum = make_float4(sum.x + t.x, sum.y + t.y, sum.z + t.z, sum.w + t.w);
-                    }
-                    v[i] = make_float4(v[i].x + sum.x, v[i].y + sum.y, v[i].z + sum.z, v[i].w + sum.w);
-                    if (group_of(b0 + i) % writers == writer)
-                        reinterpret_cast<float4*>(keep)[idx] = v[i];
+                    const float4 sm = word_sum4(a, sh, parts, ph.k, 4 * idx, tag);
+                    v[i] = make_float4(v[i].x + sm.x, v[i].y + sm.y, v[i].z + sm.z, v[i].w + sm.w);
+                    if (group_of(b0 + i) % writers == writer) reinterpret_cast<float4*>(keep)[idx] = v[i];
                 }
             }
         }
@@ -753,7 +766,9 @@ __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& s
         for (; j < ph.ipu; ++j) v4[0] += pp[j * 16];
         v = ((v4[0] + v4[1]) + (v4[2] + v4[3])) * scale;
     }
-    if (ph.kparts == 1) {
+    if (kTp && (p == 2 || p == 4)) {  // sent to every rank after the local signal (kparts == 1)
+        if (lane < 16) sh.xv[k * 16 + lane] = v;
+    } else if (ph.kparts == 1) {
         tile_epilogue<kTp>(a, p, tile, v, res);
     } else {
         if (lane < 16) a.kpart[static_cast<size_t>(kp) * ph.n + tile * 16 + lane] = v;
@@ -776,7 +791,7 @@ __device__ void finish_unit(const StackArgs& a, const Shared& sh, const Sched& s
 
 template <bool kTp>
 __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc, int l, int p, int first, int count,
-                           unsigned seq_base) {
+                           unsigned seq_base, unsigned tag_base) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const StackPhase& ph = a.ph[p];
     const int groups = ph.k >> 7;
@@ -853,15 +868,22 @@ __device__ void gemv_phase(const StackArgs& a, const Shared& sh, const Sched& sc
     }
     cbar();
     if (threadIdx.x == 0 && !failed(sh)) {
-        if (kTp && (p == 2 || p == 4)) {
-            signal_exchange(a, l, p, static_cast<unsigned>(min(sc.grid, ph.units)));
-        } else {
-            signal_phase(a, l, p);
-        }
+        signal_phase(a, l, p);
         stamp(a, l, p, 3);
         unsigned long long* w = reinterpret_cast<unsigned long long*>(sh.misc + 4);
         record(a, l, p, 5, *w);
         *w = 0;
+    }
+    if (kTp && (p == 2 || p == 4) && !failed(sh)) {
+        // the CTA's rows to every rank's exchange block, tagged, after the local signal: no
+        // release follows them (a reader checks each word's tag), so nothing waits for NVLink
+        const unsigned tag = xtag(tag_base, l);
+        unsigned long long* const* dst = p == 2 ? a.xo : a.xdown;
+        for (int i = threadIdx.x; i < count * 16; i += kConsumers) {
+            const int row = (first + (i >> 4) * sc.grid) * 16 + (i & 15);
+            const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(sh.xv[i]);
+            for (int r = 0; r < a.tp; ++r) st_word_sys(dst[r] + static_cast<size_t>(a.rank) * a.hidden + row, w);
+        }
     }
 }
 
@@ -1105,7 +1127,7 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
 }
 
 template <int G, bool kTp>
-__device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos, unsigned xtarget) {
+__device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos, unsigned tag_base) {
     const int tid = threadIdx.x;
     unsigned seq = 0;
     for (int l = 0; l < a.L; ++l) {
@@ -1118,10 +1140,7 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
             // input dependency: the phase before (layer 0's input comes from an earlier launch)
             if (l > 0 || p > 0) {
                 const int lp = p == 0 ? l - 1 : l, pp = p == 0 ? kStackPhases - 1 : p - 1;
-                if (kTp && (pp == 2 || pp == 4))  // row-parallel o / down: every rank's sums
-                    wait_exchange(a, sh, lp, pp == 4 ? 1 : 0, xtarget);
-                else
-                    wait_phase(a, sh, lp, pp, static_cast<unsigned>(min(sc.grid, sc.units(a, pp))));
+                wait_phase(a, sh, lp, pp, static_cast<unsigned>(min(sc.grid, sc.units(a, pp))));
             } else {
                 cbar();
             }
@@ -1149,44 +1168,43 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
                 const float* nw = p == 0 ? Ly.attn_norm : (p == 3 ? Ly.ffn_norm : nullptr);
                 // tensor parallel: attn_res = hidden + sum(o partials) (qwen.cpp:262) and
                 // hidden = attn_res + sum(down partials) (qwen.cpp:291), formed here
-                const float* parts = nullptr;
+                const unsigned long long* parts = nullptr;
+                unsigned tag = 0;
                 float* keep = nullptr;
                 if (kTp && p == 3) {
                     x = a.hidden_buf;
                     parts = a.xo[a.rank];
+                    tag = xtag(tag_base, l);
                     keep = a.attn_res;
                 } else if (kTp && p == 0 && l > 0) {
                     x = a.attn_res;
                     parts = a.xdown[a.rank];
+                    tag = xtag(tag_base, l - 1);
                     keep = a.hidden_buf;
                 }
-                stage_x(x, nw, ph, own, sh, parts, a.tp, keep, first, min(sc.grid, ph.units));
+                stage_x(a, x, nw, ph, own, sh, parts, tag, keep, first, min(sc.grid, ph.units));
             }
             if (own)
                 __syncwarp();
             else
                 cbar();
             if (tid == 0) stamp(a, l, p, 2);
-            gemv_phase<kTp>(a, sh, sc, l, p, first, count, seq);
+            gemv_phase<kTp>(a, sh, sc, l, p, first, count, seq, tag_base);
             seq += static_cast<unsigned>(count * ph.ipu);
         }
     }
     if (kTp) {
         // the final residual stream for the LM head: hidden = attn_res + sum(down partials)
-        // of the last layer, group g by CTA g mod grid (warp w: g = blockIdx + w grid)
-        wait_exchange(a, sh, a.L - 1, 1, xtarget);
+        // of the last layer, group g by CTA g mod grid (warp w: g = blockIdx + w grid); the
+        // local wait orders the attn_res write-back of the last gate/up staging
+        wait_phase(a, sh, a.L - 1, 4, static_cast<unsigned>(min(sc.grid, sc.units(a, 4))));
         const int lane = tid & 31, warp = tid >> 5;
         const int g = static_cast<int>(blockIdx.x) + warp * sc.grid;
         if (!failed(sh) && g < (a.hidden >> 7)) {
-            const int idx = g * 32 + lane, h4 = a.hidden >> 2;
-            const float4* p4 = reinterpret_cast<const float4*>(a.xdown[a.rank]);
-            float4 sum = __ldcg(p4 + idx);
-            for (int r = 1; r < a.tp; ++r) {
-                const float4 t = __ldcg(p4 + static_cast<size_t>(r) * h4 + idx);
-                sum = make_float4(sum.x + t.x, sum.y + t.y, sum.z + t.z, sum.w + t.w);
-            }
+            const int idx = g * 32 + lane;
+            const float4 sm = word_sum4(a, sh, a.xdown[a.rank], a.hidden, 4 * idx, xtag(tag_base, a.L - 1));
             const float4 b = __ldcg(reinterpret_cast<const float4*>(a.attn_res) + idx);
-            reinterpret_cast<float4*>(a.hidden_buf)[idx] = make_float4(b.x + sum.x, b.y + sum.y, b.z + sum.z, b.w + sum.w);
+            reinterpret_cast<float4*>(a.hidden_buf)[idx] = make_float4(b.x + sm.x, b.y + sm.y, b.z + sm.z, b.w + sm.w);
         }
     }
 }
@@ -1214,16 +1232,16 @@ __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs
         return;
     }
     const Sched sc = make_sched(a, pos);
-    // tensor parallel: this launch's exchange counters reach (epoch + 1) * tp
+    // tensor parallel: this launch's exchange tags (see StackArgs)
     const unsigned ep = kTp ? *reinterpret_cast<const volatile unsigned*>(a.epoch) : 0u;
     if (warp == W) {
         producer(a, sh, sc, pos);
     } else if (warp == W + 1) {
         prefetcher(a, sh, sc, pos);
     } else {
-        consumer<G, kTp>(a, sh, sc, pos, (ep + 1u) * static_cast<unsigned>(a.tp));
-        // every CTA read the epoch before its first signal, and CTA 0 gets here only after
-        // all ranks finished the last layer
+        consumer<G, kTp>(a, sh, sc, pos, (ep + 1u) * static_cast<unsigned>(a.L + 1));
+        // every CTA read the epoch at its start, and CTA 0 gets here only after all ranks
+        // finished the last layer
         if (kTp && blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.epoch) = ep + 1u;
     }
     pdl_launch_dependents();
@@ -1299,20 +1317,20 @@ size_t stack_sync_words(const StackArgs& a) {
 }
 
 size_t stack_exchange_bytes(int tp, int hidden, int L) {
-    return 2 * static_cast<size_t>(tp) * hidden * 4 + static_cast<size_t>(L) * 2 * 4 + 4;
+    (void)L;
+    return 2 * static_cast<size_t>(tp) * hidden * 8 + 16;
 }
 
 void stack_bind_exchange(StackArgs* a, int tp, int rank, void* const* base) {
     a->tp = tp;
     a->rank = rank;
-    const size_t part = static_cast<size_t>(tp) * a->hidden * 4;
+    const size_t part = static_cast<size_t>(tp) * a->hidden * 8;
     for (int r = 0; r < kStackMaxTp; ++r) {
         uint8_t* b = r < tp ? static_cast<uint8_t*>(base[r]) : nullptr;
-        a->xo[r] = b ? reinterpret_cast<float*>(b) : nullptr;
-        a->xdown[r] = b ? reinterpret_cast<float*>(b + part) : nullptr;
-        a->xctr[r] = b ? reinterpret_cast<unsigned*>(b + 2 * part) : nullptr;
+        a->xo[r] = b ? reinterpret_cast<unsigned long long*>(b) : nullptr;
+        a->xdown[r] = b ? reinterpret_cast<unsigned long long*>(b + part) : nullptr;
     }
-    a->epoch = a->xctr[rank] + 2 * a->L;
+    a->epoch = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(base[rank]) + 2 * part);
 }
 
 size_t stack_kpart_floats(const StackArgs& a) {
@@ -1360,8 +1378,11 @@ bool stack_plan(StackArgs* a, int grid) {
     const int xbytes = align_up(std::max(digits, att), 128);
     const int part = align_up(a->part_floats * 4, 16);
     const int ucnt = align_up(max_units * 4, 16);
+    const int xv = align_up(max_units * 16 * 4, 16);
+    // tensor parallel: o and down leave whole row sums (no split-K ticket) for the exchange
+    if (a->tp > 1 && (a->ph[2].kparts != 1 || a->ph[4].kparts != 1)) return false;
     const int misc = 32 * 4 + 32;
-    const int fixed = xbytes + part + ucnt + misc + 256;
+    const int fixed = xbytes + part + ucnt + xv + misc + 256;
     const int budget = 227 * 1024;
     int slots = (budget - fixed) / (kItemBytes + 16);
     slots = std::min(slots, 128);
@@ -1376,6 +1397,8 @@ bool stack_plan(StackArgs* a, int grid) {
     off += part;
     a->off_ucnt = off;
     off += ucnt;
+    a->off_xv = off;
+    off += xv;
     a->off_misc = off;
     off += misc;
     a->smem_bytes = align_up(off, 128);

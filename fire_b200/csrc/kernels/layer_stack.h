@@ -92,15 +92,13 @@ struct StackArgs {
     // row-parallel: each rank leaves partial row sums that every rank adds up, in rank
     // order, while staging the next phase's input. Rank r owns an exchange block (layout
     // in stack_exchange_bytes) mapped into every rank: xo[r] / xdown[r] are its o / down
-    // partials [tp][hidden], xctr[r] its counters [L][2] (o, down), each bumped once per
-    // rank per launch; epoch counts this rank's completed launches, so a wait targets
-    // (epoch + 1) * tp and the counters are never reset. The epilogues store straight
-    // into the peers' blocks; the last CTA of a rank to finish a phase (local ticket)
-    // bumps every rank's counter with a system-scope release.
+    // partials [tp][hidden] as 64-bit words (tag << 32 | float bits). A CTA stores its rows'
+    // partials into every rank's block with plain relaxed stores after its local phase
+    // signal; a reader polls each word until the tag is this launch's tag for the layer,
+    // (epoch + 1) * (L + 1) + layer + 1, with epoch = this rank's completed launches.
     int tp, rank;
-    float* xo[kStackMaxTp];
-    float* xdown[kStackMaxTp];
-    unsigned* xctr[kStackMaxTp];
+    unsigned long long* xo[kStackMaxTp];
+    unsigned long long* xdown[kStackMaxTp];
     unsigned* epoch;
     // optional timeline [grid][L][kStackPhases][kStackTraceSlots] of %globaltimer stamps:
     // 0 phase entered, 1 input dependency met, 2 input staged, 3 the CTA's last unit
@@ -117,13 +115,13 @@ struct StackArgs {
     int ring_slots;
     int max_units;    // GEMV units one CTA owns in one phase, at most
     int part_floats;  // floats of the per-item partial sums of one phase (max over phases)
-    int off_bar, off_x, off_part, off_ucnt, off_misc;
+    int off_bar, off_x, off_part, off_ucnt, off_xv, off_misc;
     int smem_bytes;
 };
 
 size_t stack_sync_words(const StackArgs& a);
-// Exchange block of one rank: o partials [tp][hidden] f32, down partials [tp][hidden]
-// f32, counters [L][2] u32, then the epoch word.
+// Exchange block of one rank: o partials [tp][hidden] and down partials [tp][hidden] as
+// tagged 64-bit words, then the epoch word.
 size_t stack_exchange_bytes(int tp, int hidden, int L);
 // Point a's exchange fields at the blocks `base[r]` (rank r's block as mapped here).
 void stack_bind_exchange(StackArgs* a, int tp, int rank, void* const* base);
