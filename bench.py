@@ -444,7 +444,8 @@ def run_ours(args):
         traffic = None
         try:
             tr = json.load(open(os.path.join(ROOT, "profiles", "dram_traffic.json")))
-            traffic = tr.get(kern_name, {}).get("bytes_per_launch_scaled")
+            # the committed capture is of the TP1 launch; no TP capture exists
+            traffic = tr.get(kern_name, {}).get("bytes_per_launch_scaled") if world == 1 else None
         except (OSError, ValueError):
             pass
         line = {
