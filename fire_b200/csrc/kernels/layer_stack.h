@@ -1,6 +1,7 @@
-// Persistent decode kernel for the whole Qwen3 layer stack (one GPU, tensor-parallel
-// size 1): the per-layer sequence of Fire's Qwen3Model::forward
-// (src/model/qwen.cpp:190-292) as one launch.
+// Persistent decode kernel for the whole Qwen3 layer stack: the per-layer sequence of
+// Fire's Qwen3Model::forward (src/model/qwen.cpp:190-292) as one launch per GPU, on one GPU
+// or on each rank of a tensor-parallel group (o/down reductions exchanged inside the
+// kernel through NVLink peer memory, see StackArgs).
 //
 // Every INT4 projection is stored as "items" of 16 rows x 256 K (2208 bytes) in the
 // order the kernel reads them. One CTA runs per SM: a producer warp streams every item
