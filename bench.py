@@ -17,8 +17,19 @@ decode from the end of the prompt, ending at context 2048.
            K/V rows it reads + norms), under tensor parallelism the INT4 GEMV on the
            decode shapes
 
+  parity = the engine's KV prefix (positions 0..1790 after the prefill) is exported into
+           the oracle (the FP32 CPU restatement of Qwen3Model::forward, oracle/), which then
+           decodes the same 256 steps fed the GPU's tokens: every sampled id must equal the
+           oracle's argmax, and the logits of the first steps are compared (rel-L2, max |d|)
+  gemv_sweep = the INT4 group-128 GEMV at M=1 on every Qwen3-8B projection shape and the
+           BF16 LM head (seed-0 RTN N(0,0.02) weights, FP16-valued scales), working sets
+           larger than L2, GB/s against the measured HBM peak; plus the 3072x1024 single
+           Linear (L2-resident, microseconds) beside the CPU FP32 Linear on the dequantised
+           weights
+
 `--impl reference` times the CPU restatement of the same decode (oracle/, FP32 on the
 host cores) on a bounded sample of the workload (see `cpu_baseline.sample`).
+`--gemv` runs only the GEMV sweep (it sizes the ncu captures of the GEMV kernels).
 """
 from __future__ import annotations
 
@@ -56,6 +67,9 @@ def parse():
     ap.add_argument("--gen", type=int, default=GEN, help="greedy tokens per step")
     ap.add_argument("--prefill", action="store_true",
                     help="only the M=512 INT4 prefill GEMM sweep over the 8B projection shapes")
+    ap.add_argument("--gemv", action="store_true",
+                    help="only the M=1 INT4 / BF16 GEMV sweep over the 8B decode shapes")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle parity leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers (0 = the model's 36); fewer only to size an ncu capture")
     return ap.parse_args()
@@ -126,31 +140,6 @@ class ClockSampler:
 
 # ------------------------------------------------------------ CPU baseline ----
 
-def cpu_decode_sample(profile, weights_np, budget_s: float = 20.0, min_tokens: int = 1, pos0: int = PROMPT - 1):
-    """Time the oracle (FP32 CPU restatement of Qwen3Model::forward) decoding tokens at
-    the workload's context (KV positions 0..pos0-1 filled with values ~N(0,1)); stops
-    after `budget_s` seconds of decoding. Returns (tokens/s, tokens timed, threads)."""
-    from oracle import oracle as O
-
-    O.set_threads(os.cpu_count() or 1)
-    m = O.Qwen3Oracle(profile, weights_np, capacity=CAPACITY)
-    rng = np.random.default_rng(1)
-    m.kc[:, :pos0] = rng.standard_normal(m.kc[:, :pos0].shape, dtype=np.float32)
-    m.vc[:, :pos0] = rng.standard_normal(m.vc[:, :pos0].shape, dtype=np.float32)
-    m.length = pos0
-    tok, n, t0 = 1234, 0, time.perf_counter()
-    while True:
-        lg = m.forward(tok, pos0 + n)
-        tok = int(np.argmax(lg))
-        n += 1
-        if n >= min_tokens and time.perf_counter() - t0 >= budget_s:
-            break
-        if n >= 8:
-            break
-    dt = time.perf_counter() - t0
-    return n / dt, n, O.lib().fo_get_threads()
-
-
 def host_weights(weights_dev):
     """Device checkpoint (torch) -> host numpy arrays in Fire's wire dtypes."""
     import torch
@@ -166,6 +155,9 @@ def host_weights(weights_dev):
 
 
 # ------------------------------------------------------------ reference arm ----
+
+REF_TOKENS_PER_STEP = 4
+
 
 def run_reference(args):
     rank, _, world = dist_env()
@@ -190,15 +182,23 @@ def run_reference(args):
     m.vc[:, :pos0] = rng.standard_normal(m.vc[:, :pos0].shape, dtype=np.float32)
     m.length = pos0
     tok = 1234
-    for i in range(args.warmup):  # each step: one greedy decode token at context ~1792
-        m.length = pos0
-        tok = int(np.argmax(m.forward(tok, pos0)))
+    gen = CAPACITY - pos0
+
+    def step(i):
+        # REF_TOKENS_PER_STEP greedy tokens; successive steps walk the decode range 1791..2047
+        nonlocal tok
+        start = (i * REF_TOKENS_PER_STEP) % (gen - REF_TOKENS_PER_STEP)
+        m.length = pos0 + start
+        for j in range(REF_TOKENS_PER_STEP):
+            tok = int(np.argmax(m.forward(tok, m.length)))
+
+    for i in range(args.warmup):
+        step(i)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        m.length = pos0 + (i % (CAPACITY - pos0))
-        tok = int(np.argmax(m.forward(tok, m.length)))
+        step(args.warmup + i)
     dt = time.perf_counter() - t0
-    val = args.steps / dt
+    val = args.steps * REF_TOKENS_PER_STEP / dt
     cores = O.lib().fo_get_threads()
     line = {"metric": METRIC, "value": val, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True,
@@ -207,8 +207,9 @@ def run_reference(args):
             "config": {"workload": "qwen3-8b-w4-decode-ctx2048", "layout": "mixed (INT4 g128 + BF16 head)",
                        "layers": 36, "context": CAPACITY},
             "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": "one greedy decode token per step at context 1792 (KV prefix N(0,1)), "
-                                       "FP32 dequantised INT4 on the fly, all 36 layers + BF16 head"},
+                             "sample": f"{REF_TOKENS_PER_STEP} greedy decode tokens per step, successive steps "
+                                       "walking positions 1791..2047 (KV prefix N(0,1)); FP32 dequantised INT4 on "
+                                       "the fly, all 36 layers + BF16 head"},
             "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -262,6 +263,162 @@ def time_w4_gemv(stream, reps: int = 4):
     return by / launches, ms * 1e3 / launches  # bytes per launch, us per launch
 
 
+GEMV_SHAPES = [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+               ("gate", 12288, 4096), ("up", 12288, 4096), ("down", 4096, 12288),
+               ("qkv_fused", 6144, 4096), ("gate_up_fused", 24576, 4096)]
+L2_BYTES = 126 * 1024 * 1024
+
+
+def gemv_sweep(reps_min: int = 100):
+    """fire_b200_linear_w4 (M=1, group 128) on every Qwen3-8B projection shape, and
+    fire_b200_linear_dense on the BF16 LM head. Weights: W ~ N(0, 0.02) from a seeded
+    generator, RTN INT4 (the reference rule), scales rounded to FP16 values; x ~ N(0, 1).
+    Each shape is replicated until the copies exceed twice the L2, and the launches cycle
+    through the copies (every launch streams its matrix from HBM); >= reps_min launches in
+    a CUDA graph, timed with CUDA events. Bytes per launch = N*K/2 + N*K/128*(4+1) + 4K + 4N
+    (INT4) or 2*N*K + 4K + 4N (BF16)."""
+    import torch
+
+    from fire_b200 import _native as N
+    from fire_b200.quant import quantize_torch
+
+    L = N.lib()
+    peak = float(peaks().get("hbm_gbs", 6650.0))
+    stream = torch.cuda.Stream()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0)
+    out = []
+
+    def timed(launch, copies):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            for c in range(copies):
+                launch(c)
+            with torch.cuda.graph(graph, stream=stream):
+                for c in range(copies):
+                    launch(c)
+            for _ in range(3):
+                graph.replay()
+            reps = max(1, -(-reps_min // copies))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        stream.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / (reps * copies), reps * copies
+
+    for name, n, k in GEMV_SHAPES:
+        w = torch.empty(n, k, device="cuda").normal_(0.0, 0.02, generator=gen)
+        x = torch.empty(k, device="cuda").normal_(0.0, 1.0, generator=gen)
+        q, sc, z = quantize_torch(w, 128)
+        del w
+        sc = sc.to(torch.float16).to(torch.float32)
+        by = n * k // 2 + n * (k // 128) * 5 + 4 * k + 4 * n
+        copies = max(1, -(-2 * L2_BYTES // by))
+        mats = [(q.clone(), sc.clone(), z.clone()) for _ in range(copies)]
+        y = torch.empty(n, device="cuda")
+
+        def launch(c, mats=mats, x=x, y=y, n=n, k=k):
+            qq, ss, zz = mats[c]
+            rc = L.fire_b200_linear_w4(x.data_ptr(), qq.data_ptr(), ss.data_ptr(), zz.data_ptr(), y.data_ptr(), 1,
+                                       n, k, 128, stream.cuda_stream)
+            assert rc == 0, rc
+
+        us, launches = timed(launch, copies)
+        gbs = by / (us * 1e3)
+        out.append({"name": name, "n": n, "k": k, "bytes": by, "us": round(us, 2), "gbs": round(gbs, 1),
+                    "frac": round(gbs / peak, 3), "launches": launches, "copies": copies})
+        del mats, q, sc, z
+    n, k = 151936, 4096
+    w = (torch.empty(n, k, device="cuda").normal_(0.0, 0.02, generator=gen)).to(torch.bfloat16)
+    x = torch.empty(k, device="cuda").normal_(0.0, 1.0, generator=gen)
+    y = torch.empty(n, device="cuda")
+    by = 2 * n * k + 4 * k + 4 * n
+
+    def launch_head(c):
+        rc = L.fire_b200_linear_dense(x.data_ptr(), w.data_ptr(), N.BF16, 1.0, y.data_ptr(), 1, n, k,
+                                      stream.cuda_stream)
+        assert rc == 0, rc
+
+    us, launches = timed(launch_head, 1)
+    gbs = by / (us * 1e3)
+    head = {"name": "lm_head_bf16", "n": n, "k": k, "bytes": by, "us": round(us, 2), "gbs": round(gbs, 1),
+            "frac": round(gbs / peak, 3), "launches": launches}
+    del w
+    big = [r for r in out if r["bytes"] > 20e6] + [head]
+    return {"shapes": out, "lm_head": head, "peak_gbs": peak,
+            "large_shape_frac": round(sum(r["bytes"] for r in big) / sum(r["bytes"] / r["frac"] for r in big), 3),
+            "kernels": "w4g128 K-specialised streaming GEMV (INT4); dense_gemv_kernel (BF16 head)",
+            "l2": "copies of each matrix cycled, >= 2x L2 (126 MB) per cycle"}
+
+
+def single_linear(reps: int = 1000):
+    """The 3072x1024 single Linear (seed-0 N(0,0.02) RTN INT4 weights, x ~ N(0,1) drawn after
+    W): the GPU INT4 GEMV in microseconds (L2-resident, median of per-call CUDA-event times
+    of graph replays), beside the CPU FP32 Linear on the dequantised weights."""
+    import torch
+
+    from fire_b200 import _native as N
+    from fire_b200 import quant
+
+    rng = np.random.default_rng(0)
+    W = rng.normal(0, 0.02, (3072, 1024)).astype(np.float32)
+    x = rng.normal(0, 1, (1, 1024)).astype(np.float32)[0]
+    q, s, z = quant.quantize_int4_groupwise(W, 128)
+    p = quant.pack_uint4(q)
+    L = N.lib()
+    dq, ds, dz, dx = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (p, s, z, x))
+    y = torch.empty(3072, device="cuda")
+    stream = torch.cuda.Stream()
+    per_graph = 20
+
+    def call():
+        rc = L.fire_b200_linear_w4(dx.data_ptr(), dq.data_ptr(), ds.data_ptr(), dz.data_ptr(), y.data_ptr(), 1,
+                                   3072, 1024, 128, stream.cuda_stream)
+        assert rc == 0, rc
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        call()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(per_graph):
+                call()
+        graph.replay()
+        times = []
+        for _ in range(reps // per_graph):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3 / per_graph)
+    gpu_us = statistics.median(times)
+    return {"shape": [3072, 1024], "gpu_us": round(gpu_us, 3),
+            "note": "L2-resident (1.7 MB); launch-bound, not a roofline case"}, (x, p, s, z)
+
+
+def cpu_linear(x, p, s, z, reps: int = 1000):
+    """Fire's CPU FP32 Linear on the dequantised weights (src/op/kernels/cpu/matmul_kernel.cpp,
+    restated by the oracle), median microseconds per call on all host threads and on one."""
+    from oracle import oracle as O
+
+    w = O.dequant_int4(p, s, z, 128)
+    res = {}
+    for threads in (os.cpu_count() or 1, 1):
+        O.set_threads(threads)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            O.linear_f32(x, w)
+            ts.append(time.perf_counter() - t0)
+        res[threads] = statistics.median(ts) * 1e6
+    O.set_threads(os.cpu_count() or 1)
+    allc = os.cpu_count() or 1
+    return {"cpu_fp32_us": round(res[allc], 2), "cpu_cores": allc, "cpu_fp32_us_1core": round(res[1], 2),
+            "kind": "port"}
+
+
 PREFILL_M = 512
 PREFILL_SHAPES = [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)]  # q/k/v, o, gate/up, down
 
@@ -313,6 +470,76 @@ def prefill_sweep(reps: int = 10):
             "note": "per call: W dequant to BF16 + x hi/lo split + tcgen05 GEMM (2 BF16 MMAs per K16)"}
 
 
+def parity_leg(eng, p, wn, pos0, first, gpu_tokens, world, rank, logit_steps: int = 4):
+    """Greedy-token identity against the oracle from the engine's own KV prefix.
+
+    Every rank exports its KV shard (positions < pos0); rank 0 assembles the full cache
+    (heads in rank order) into the oracle and decodes the GPU's 256 steps, fed the GPU's
+    tokens: each GPU token must be the oracle's argmax. The first `logit_steps` logits are
+    compared too (all ranks run those forwards: under tensor parallelism they are
+    collective). Returns (parity dict, cpu tokens/s over the first ~20 s, tokens timed)
+    on rank 0, (None, None, None) elsewhere."""
+    import torch
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+
+    kc, vc = eng.kv_export(pos0)
+    logits = torch.empty(p.vocab_size, device="cuda")
+    eng.truncate(pos0)
+    gpu_logits = []
+    tok = first
+    for i in range(logit_steps):
+        eng.forward(tok, pos0 + i, logits)
+        torch.cuda.synchronize()
+        gpu_logits.append(logits.cpu().numpy().copy())
+        tok = gpu_tokens[i]
+    if world > 1:
+        kt, vt = torch.from_numpy(kc), torch.from_numpy(vc)
+        kl = [torch.empty_like(kt) for _ in range(world)] if rank == 0 else None
+        vl = [torch.empty_like(vt) for _ in range(world)] if rank == 0 else None
+        dist.gather(kt, kl, dst=0)
+        dist.gather(vt, vl, dst=0)
+        if rank == 0:
+            kc = np.concatenate([t.numpy() for t in kl], axis=2)
+            vc = np.concatenate([t.numpy() for t in vl], axis=2)
+    if rank != 0:
+        return None, None, None
+    O.set_threads(os.cpu_count() or 1)
+    ref = O.Qwen3Oracle(p, wn, capacity=CAPACITY)
+    ref.kc[:, :pos0] = kc
+    ref.vc[:, :pos0] = vc
+    ref.length = pos0
+    tok = first
+    mism, rels, absd, margins = [], [], [], []
+    t0 = time.perf_counter()
+    cpu_n, cpu_s = 0, None
+    for i in range(len(gpu_tokens)):
+        lg = ref.forward(tok, pos0 + i)
+        if cpu_s is None:
+            cpu_n += 1
+            if time.perf_counter() - t0 >= 20.0:
+                cpu_s = time.perf_counter() - t0
+        top2 = np.partition(lg, -2)[-2:]
+        margins.append(float(top2[1] - top2[0]))
+        if int(np.argmax(lg)) != int(gpu_tokens[i]):
+            mism.append(i)
+        if i < logit_steps:
+            g = gpu_logits[i]
+            rels.append(float(np.linalg.norm(g - lg) / np.linalg.norm(lg)))
+            absd.append(float(np.max(np.abs(g - lg))))
+        tok = int(gpu_tokens[i])
+    if cpu_s is None:
+        cpu_s = time.perf_counter() - t0
+    parity = {"tokens_equal": not mism, "steps": len(gpu_tokens), "first_mismatch": mism[0] if mism else None,
+              "logit_steps": logit_steps, "max_rel_l2": max(rels), "max_abs_diff": max(absd),
+              "min_top2_margin": min(margins),
+              "prefix": f"the engine's KV cache of positions 0..{pos0 - 1} (after its prefill), exported to the "
+                        f"oracle; the oracle is fed the GPU's tokens and must pick each of them",
+              "bar": "ids identical; logits rel-L2 < 1e-4, max |d| < 1e-2 (test_qwen_profile.cpp:451-453)"}
+    return parity, cpu_n / cpu_s, cpu_n
+
+
 def layer_stack_bytes(p, world: int, pos: int) -> float:
     """Algorithmic HBM bytes of one layer-stack launch at position `pos`: per layer the
     INT4 q/k/v, o, gate/up and down matrices (0.5 B per weight, 4 B scale + 1 B zero point
@@ -354,7 +581,7 @@ def run_ours(args):
     w = synth.generate_torch(p, "mixed", seed=0, device="cuda")
     eng = Qwen3Engine(p, w, tp_rank=rank, tp_size=world, nccl_id=nid)
     cpu_w = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and not args.no_parity:
         cpu_w = host_weights(w)
     del w
     torch.cuda.empty_cache()
@@ -428,12 +655,22 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e, kern_us = t.tolist()
     clocks = clk.summary()
-    cpu = None
-    if cpu_w is not None:
-        tps, n, cores = cpu_decode_sample(p, cpu_w)
-        cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
-               "sample": f"{n} greedy decode tokens at context 1791+ (KV prefix N(0,1)) through the FP32 CPU "
-                         f"restatement of Qwen3Model::forward, INT4 dequantised on the fly, all 36 layers"}
+    cpu = parity = None
+    if not args.no_parity:
+        parity, tps, n = parity_leg(eng, p, cpu_w, n_prompt - 1, first, ref_tokens, world, rank)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as O
+
+            cpu = {"value": tps, "unit": "tok/s", "cores": O.lib().fo_get_threads(), "kind": "port",
+                   "sample": f"the first {n} greedy decode steps (about 20 s) of the parity leg: the FP32 CPU "
+                             f"restatement of Qwen3Model::forward from the engine's KV prefix at position "
+                             f"{n_prompt - 1}, INT4 dequantised on the fly, all 36 layers + BF16 head"}
+    gemv = lin = None
+    if rank == 0 and world == 1:
+        gemv = gemv_sweep()
+        lin, lin_data = single_linear()
+        if not args.no_cpu_baseline:
+            lin.update(cpu_linear(*lin_data))
     if rank == 0:
         pk = peaks()
         peak = float(pk.get("hbm_gbs", 6650.0))
@@ -458,7 +695,7 @@ def run_ours(args):
                        "parallelism": f"tp{world}", "layers": p.num_layers,
                        "l2": "weights 4.99 GB/token > 126 MB L2 (no flush needed)"},
             "e2e": {"value": tok_s_e2e, "unit": "tok/s", "h2d_bytes_per_step": 16 * n_gen,
-                    "d2h_bytes_per_step": 4 * n_gen},
+                    "d2h_bytes_per_step": 16 * n_gen},
             "gpu_launches": (eng.kernels_per_step * n_gen + 1) * args.steps,
             "roofline": {"bound": "hbm", "kernel": kern_name, "achieved": kern_bytes / (kern_us * 1e3),
                          "peak": peak, "unit": "GB/s", "frac": kern_bytes / (kern_us * 1e3) / peak,
@@ -472,6 +709,11 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
+        if gemv is not None:
+            line["gemv_sweep"] = gemv
+            line["single_linear"] = lin
         line["prefill"] = {"prompt_tokens": n_prompt - 1, "ms": round(prefill_ms, 2),
                            "tok_s": round((n_prompt - 1) / (prefill_ms / 1e3), 1) if prefill_ms > 0 else None,
                            "path": "batched tcgen05 prefill" if world == 1 else "forward() per token",
@@ -495,6 +737,13 @@ def main():
         torch.cuda.set_device(0)
         print(json.dumps({"metric": "INT4 prefill GEMM TFLOP/s (M=512, Qwen3-8B projection shapes)",
                           **prefill_sweep()}), flush=True)
+        return 0
+    if args.gemv:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"metric": "INT4 GEMV HBM GB/s vs peak (M=1, Qwen3-8B shapes)", **gemv_sweep(),
+                          "single_linear": single_linear()[0]}), flush=True)
         return 0
     return run_ours(args)
 

@@ -18,7 +18,7 @@ class Tensor(C.Structure):
 
 class Options(C.Structure):
     _fields_ = [("tp_rank", C.c_int), ("tp_size", C.c_int), ("nccl_id", C.c_void_p), ("use_graph", C.c_int),
-                ("pdl", C.c_int)]
+                ("pdl", C.c_int), ("deadline_ms", C.c_int)]
 
 
 _vp, _i = C.c_void_p, C.c_int
@@ -32,6 +32,10 @@ SIGNATURES: dict = {
     "fire_b200_qwen3_generate": (_i, [_vp, _i, _i, _vp, _vp]),
     "fire_b200_qwen3_generate_host": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "fire_b200_qwen3_reset": (_i, [_vp]),
+    "fire_b200_qwen3_status": (_i, [_vp, C.POINTER(C.c_int)]),
+    "fire_b200_qwen3_abort": (_i, [_vp]),
+    "fire_b200_qwen3_kv_export": (_i, [_vp, _i, _vp, _vp, _vp]),
+    "fire_b200_qwen3_kv_import": (_i, [_vp, _i, _vp, _vp, _vp]),
     "fire_b200_qwen3_truncate": (_i, [_vp, _i]),
     "fire_b200_qwen3_length": (_i, [_vp]),
     "fire_b200_qwen3_logits": (_vp, [_vp]),

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(PKG, "libfire_b200.so")
 HEADER = os.path.join(ROOT, "include", "fire_b200.h")
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_NO_DEVICE, ERR_STATE, ERR_IO, ERR_NOMEM = 0, -1, -2, -3, -4, -5, -6
+ERR_DEVICE, ERR_TIMEOUT = -7, -8
 F32, BF16 = 0, 1
 
 

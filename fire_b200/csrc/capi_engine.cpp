@@ -40,6 +40,7 @@ fb::EngineOptions options(const fire_b200_qwen3_options* o) {
         eo.nccl_id = o->nccl_id;
         eo.use_graph = o->use_graph != 0;
         eo.pdl = o->pdl != 0;
+        eo.deadline_ms = o->deadline_ms;
     }
     return eo;
 }
@@ -134,6 +135,16 @@ int fire_b200_qwen3_generate_host(fire_b200_qwen3* m, const int32_t* prompt, int
 }
 
 int fire_b200_qwen3_reset(fire_b200_qwen3* m) { return m ? m->e->reset() : FIRE_B200_ERR_INVALID; }
+int fire_b200_qwen3_status(fire_b200_qwen3* m, int* device_error) {
+    return m ? m->e->status(device_error) : FIRE_B200_ERR_INVALID;
+}
+int fire_b200_qwen3_abort(fire_b200_qwen3* m) { return m ? m->e->abort() : FIRE_B200_ERR_INVALID; }
+int fire_b200_qwen3_kv_export(const fire_b200_qwen3* m, int length, float* key, float* value, void* stream) {
+    return m ? m->e->kv_export(length, key, value, static_cast<cudaStream_t>(stream)) : FIRE_B200_ERR_INVALID;
+}
+int fire_b200_qwen3_kv_import(fire_b200_qwen3* m, int length, const float* key, const float* value, void* stream) {
+    return m ? m->e->kv_import(length, key, value, static_cast<cudaStream_t>(stream)) : FIRE_B200_ERR_INVALID;
+}
 int fire_b200_qwen3_truncate(fire_b200_qwen3* m, int length) {
     return m ? m->e->truncate(length) : FIRE_B200_ERR_INVALID;
 }

@@ -34,6 +34,8 @@ const char* fire_b200_status_string(int status) {
     case FIRE_B200_ERR_STATE: return "invalid state";
     case FIRE_B200_ERR_IO: return "checkpoint I/O or format error";
     case FIRE_B200_ERR_NOMEM: return "out of device memory";
+    case FIRE_B200_ERR_DEVICE: return "a kernel reported a failed step (reset the engine)";
+    case FIRE_B200_ERR_TIMEOUT: return "host deadline ran out (communicator aborted)";
     default:
         return status > 0 ? cudaGetErrorString(static_cast<cudaError_t>(status)) : "unknown status";
     }

@@ -2,9 +2,9 @@
 // cannot allocate device memory and cannot hand over a workspace.
 //
 // Some callers only ever pass the tensors they already own: a plug-in behind an
-// interface like Fire's MHAKernel (q, caches, score, output - no scratch argument),
-// or a host program whose device memory is planned once at start-up so that nothing
-// may be allocated afterwards. This entry point serves them by keeping the split-K
+// interface that hands over only the query, the caches, the score buffer and the output
+// (no scratch argument), or a host program whose device memory is planned once at
+// start-up so that nothing may be allocated afterwards. This entry point serves them by keeping the split-K
 // scratch (per-chunk partial outputs and the per-KV-head tickets) in a fixed array
 // in device memory that belongs to the library itself.
 //
@@ -12,8 +12,11 @@
 // loaded, until the process exits. In host code its name stands for a host-side
 // symbol, not a device address, so the device address is looked up with
 // cudaGetSymbolAddress once per device (with that device current) and passed to the
-// kernel. Every call shares the array: calls that overlap on the GPU (concurrent
-// streams, or several host threads) race on it and must be serialised by the caller.
+// kernel. The looked-up address is cached for the life of the process: a
+// cudaDeviceReset invalidates it, so the entry point must not be used on a device after
+// that device was reset. Every call shares the array: calls that overlap on the GPU
+// (concurrent streams, or several host threads) race on it and must be serialised by
+// the caller.
 #include <cuda_runtime.h>
 
 #include <cmath>

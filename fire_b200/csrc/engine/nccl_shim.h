@@ -12,6 +12,7 @@ namespace fb {
 using NcclComm = void*;
 constexpr int kNcclIdBytes = 128;
 enum NcclType : int { kNcclUint8 = 1, kNcclInt32 = 2, kNcclFloat32 = 7 };
+constexpr int kNcclInProgress = 7;  // ncclResult_t ncclInProgress (non-blocking operation still running)
 
 struct Nccl {
     int (*GetUniqueId)(void* id) = nullptr;

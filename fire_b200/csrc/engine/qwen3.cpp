@@ -4,6 +4,8 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <chrono>
+#include <thread>
 #include <unordered_map>
 
 #include "device_info.h"
@@ -67,11 +69,17 @@ Qwen3Engine::~Qwen3Engine() {
     if (graph_fwd_) cudaGraphExecDestroy(graph_fwd_);
     if (graph_step_) cudaGraphExecDestroy(graph_step_);
     if (host_state_) cudaFreeHost(host_state_);
-    if (host_token_) cudaFreeHost(host_token_);
+    if (host_seen_) cudaFreeHost(host_seen_);
+    if (steps_done_) cudaEventDestroy(steps_done_);
     for (int r = 0; r < kStackMaxTp; ++r)
         if (xchg_peer_[r] && xchg_peer_[r] != xchg_) cudaIpcCloseMemHandle(xchg_peer_[r]);
     if (xchg_) cudaFree(xchg_);
-    if (comm_ && nccl().ok) nccl().CommDestroy(comm_);
+    if (comm_ && nccl().ok) {
+        if (aborted_)
+            nccl().CommAbort(comm_);
+        else
+            nccl().CommDestroy(comm_);
+    }
 }
 
 // Tensor parallel with the layer stack: allocate this rank's exchange block, share its
@@ -163,6 +171,10 @@ int Qwen3Engine::create(const Qwen3Dims& d, const std::vector<TensorSrc>& tensor
             e->stack_ = stack_plan(&probe, e->sms_);
             const char* tr = std::getenv("FIRE_B200_STACK_TRACE");
             e->stack_trace_on_ = e->stack_ && tr != nullptr && std::strcmp(tr, "1") == 0;
+            // failure injection for tests: the first step after prepare (and every step
+            // until reset) fails in a bounded wait of the layer-stack kernel
+            const char* st = std::getenv("FIRE_B200_FAULT_STALL");
+            e->stall_on_ = e->stack_ && st != nullptr && std::strcmp(st, "1") == 0;
         }
         if (e->stack_ && t > 1) {
             const int xr = e->setup_exchange(err);
@@ -416,7 +428,7 @@ int Qwen3Engine::prepare(int capacity) {
         sa = stack_template(capacity);
         if (!stack_plan(&sa, sms_)) return FIRE_B200_ERR_UNSUPPORTED;
         stack_trace_words_ = stack_trace_on_ ? size_t(sa.grid) * d_.layers * kStackPhases * kStackTraceSlots : 0;
-        stack_bytes = pad256(stack_trace_words_ * 8) + pad256(stack_sync_words(sa) * 4) + pad256(stack_kpart_floats(sa) * 4 + 4) +
+        stack_bytes = 256 + pad256(stack_trace_words_ * 8) + pad256(stack_sync_words(sa) * 4) + pad256(stack_kpart_floats(sa) * 4 + 4) +
                       pad256(size_t(hq_) * sa.max_chunks * 128 * 4) + pad256(size_t(hq_) * sa.max_chunks * 2 * 4) + 1024;
     }
     size_t total = 0;
@@ -471,6 +483,13 @@ int Qwen3Engine::prepare(int capacity) {
         sa.sync = stack_sync_;
         if (tp_ > 1) stack_bind_exchange(&sa, tp_, rank_, xchg_peer_);
         sa.trace = nullptr;
+        sa.stall = nullptr;
+        if (stall_on_) {
+            stall_ = static_cast<int*>(A(sizeof(int)));
+            if (!stall_) return FIRE_B200_ERR_NOMEM;
+            FB_CK(cudaMemset(stall_, 0, sizeof(int)));  // armed below, after the checking step
+            sa.stall = stall_;
+        }
         if (stack_trace_words_) {
             sa.trace = static_cast<unsigned long long*>(A(stack_trace_words_ * 8));
             if (!sa.trace) return FIRE_B200_ERR_NOMEM;
@@ -478,7 +497,9 @@ int Qwen3Engine::prepare(int capacity) {
         stack_args_ = sa;
     }
     if (!host_state_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_state_), sizeof(DecodeState)));
-    if (!host_token_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_token_), sizeof(int32_t)));
+    if (!host_seen_) FB_CK(cudaMallocHost(reinterpret_cast<void**>(&host_seen_), sizeof(DecodeState)));
+    if (!steps_done_) FB_CK(cudaEventCreateWithFlags(&steps_done_, cudaEventDisableTiming));
+    *host_seen_ = DecodeState{0, 0, 0, 0};
 
     cudaStream_t s;
     FB_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
@@ -500,21 +521,18 @@ int Qwen3Engine::prepare(int capacity) {
         FB_RC(capture(false, &graph_fwd_));
         FB_RC(capture(true, &graph_step_));
     }
+    if (stall_) {
+        const int one = 1;
+        FB_CK(cudaMemcpy(stall_, &one, sizeof(int), cudaMemcpyHostToDevice));
+    }
     return 0;
 }
 
+// The layer-stack kernel is always launched cooperative, captured or not: its CTAs wait on
+// one another, so all of them must be resident at once, which only the cooperative launch
+// guarantees. A runtime that refuses it makes prepare() fail (the kernel is never run as a
+// plain launch).
 int Qwen3Engine::capture(bool sample, cudaGraphExec_t* exec) {
-    for (int attempt = 0;; ++attempt) {
-        const int rc = capture_once(sample, exec);
-        // a runtime that cannot capture a cooperative launch gets a plain one (one CTA per
-        // SM is resident either way: the kernel's shared memory admits no second CTA)
-        if (rc == 0 || !stack_ || !stack_coop_ || attempt > 0) return rc;
-        (void)cudaGetLastError();
-        stack_coop_ = false;
-    }
-}
-
-int Qwen3Engine::capture_once(bool sample, cudaGraphExec_t* exec) {
     cudaStream_t cs;
     FB_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
     cudaGraph_t g = nullptr;
@@ -553,13 +571,10 @@ int Qwen3Engine::enqueue_step(cudaStream_t s, bool sample) {
     if (stack_) {
         FB_CK(cudaMemsetAsync(stack_sync_, 0, stack_sync_bytes_, s));
         if (stack_args_.trace) FB_CK(cudaMemsetAsync(stack_args_.trace, 0, stack_trace_words_ * 8, s));
-        cudaError_t e = stack_launch(stack_args_, s, stack_coop_);
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (e != cudaSuccess && stack_coop_ && cudaStreamIsCapturing(s, &cs) == cudaSuccess &&
-            cs == cudaStreamCaptureStatusNone) {
+        const cudaError_t e = stack_launch(stack_args_, s, true);
+        if (e == cudaErrorCooperativeLaunchTooLarge || e == cudaErrorNotSupported) {
             (void)cudaGetLastError();
-            stack_coop_ = false;
-            e = stack_launch(stack_args_, s, false);
+            return FIRE_B200_ERR_UNSUPPORTED;  // co-residency of the CTAs cannot be guaranteed
         }
         FB_CK(e);
     }
@@ -721,7 +736,7 @@ int Qwen3Engine::time_layer_stack(int reps, float* ms_out, cudaStream_t s) {
     for (int i = 0; i <= reps && rc == 0; ++i) {  // launch 0 warms up
         if (i == 1) rc = static_cast<int>(cudaEventRecord(e0, s));
         if (!rc) rc = static_cast<int>(cudaMemsetAsync(stack_sync_, 0, stack_sync_bytes_, s));
-        if (!rc) rc = static_cast<int>(stack_launch(stack_args_, s, stack_coop_));
+        if (!rc) rc = static_cast<int>(stack_launch(stack_args_, s, true));
     }
     if (!rc) rc = static_cast<int>(cudaEventRecord(e1, s));
     if (!rc) rc = static_cast<int>(cudaEventSynchronize(e1));
@@ -764,13 +779,104 @@ StackArgs Qwen3Engine::stack_template(int capacity) const {
 
 int Qwen3Engine::forward(int token, int pos, float* logits_out, cudaStream_t s) {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    FB_RC(refuse());
     if (token < 0 || token >= d_.vocab) return FIRE_B200_ERR_INVALID;
     if (pos != length_ || pos < 0 || pos >= capacity_) return FIRE_B200_ERR_STATE;
     FB_CK(set_state_launch(state_, token, pos, 0, s, false));
     FB_RC(launch_step(s, false));
     if (logits_out != nullptr && logits_out != logits())
         FB_CK(cudaMemcpyAsync(logits_out, logits(), size_t(d_.vocab) * 4, cudaMemcpyDeviceToDevice, s));
+    FB_RC(mark_steps(s));
     ++length_;  // KVCache::commit (src/model/kv_cache.cpp:76-83)
+    return 0;
+}
+
+int Qwen3Engine::mark_steps(cudaStream_t s) {
+    FB_CK(cudaMemcpyAsync(host_seen_, state_, sizeof(DecodeState), cudaMemcpyDeviceToHost, s));
+    FB_CK(cudaEventRecord(steps_done_, s));
+    return 0;
+}
+
+int Qwen3Engine::refuse() const {
+    if (aborted_) return FIRE_B200_ERR_TIMEOUT;
+    // the mirror holds the state after the last step group that has completed (a copy
+    // still in flight shows the earlier value; status() waits for it)
+    const int err = *reinterpret_cast<const volatile int32_t*>(&host_seen_->error);
+    return err != 0 ? FIRE_B200_ERR_DEVICE : 0;
+}
+
+int Qwen3Engine::wait_event(cudaEvent_t ev) {
+    if (tp_ == 1 || comm_ == nullptr) return static_cast<int>(cudaEventSynchronize(ev));
+    // Tensor parallel: a peer that stopped answering leaves this rank's collective (or its
+    // exchange polls) unfinished; wait with a deadline, watching the communicator, and
+    // abort it when the deadline passes (ncclCommAbort ends its kernels).
+    const long long limit_ms = opt_.deadline_ms > 0 ? opt_.deadline_ms : 30000;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(ev);
+        if (q == cudaSuccess) return 0;
+        if (q != cudaErrorNotReady) return static_cast<int>(q);
+        int async_err = 0;
+        if (nccl().CommGetAsyncError(comm_, &async_err) == 0 && async_err != 0 && async_err != kNcclInProgress) {
+            nccl().CommAbort(comm_);
+            comm_ = nullptr;
+            aborted_ = true;
+            return FIRE_B200_ERR_TIMEOUT;
+        }
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+        if (ms.count() > limit_ms) {
+            nccl().CommAbort(comm_);
+            comm_ = nullptr;
+            aborted_ = true;
+            return FIRE_B200_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+int Qwen3Engine::status(int* device_error) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (aborted_) return FIRE_B200_ERR_TIMEOUT;
+    FB_RC(wait_event(steps_done_));
+    const int err = host_seen_->error;
+    if (device_error) *device_error = err;
+    return err != 0 ? FIRE_B200_ERR_DEVICE : 0;
+}
+
+int Qwen3Engine::abort() {
+    if (comm_ != nullptr && nccl().ok) {
+        nccl().CommAbort(comm_);
+        comm_ = nullptr;
+        aborted_ = true;
+    }
+    return 0;
+}
+
+int Qwen3Engine::kv_export(int length, float* key, float* value, cudaStream_t s) const {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (!key || !value || length < 0 || length > length_) return FIRE_B200_ERR_INVALID;
+    const size_t row = size_t(kv_) * 4, part = size_t(length) * row;
+    for (int l = 0; l < d_.layers; ++l) {
+        const size_t src = size_t(l) * capacity_ * kv_;
+        FB_CK(cudaMemcpyAsync(reinterpret_cast<char*>(key) + l * part, kcache_ + src, part, cudaMemcpyDefault, s));
+        FB_CK(cudaMemcpyAsync(reinterpret_cast<char*>(value) + l * part, vcache_ + src, part, cudaMemcpyDefault, s));
+    }
+    FB_CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int Qwen3Engine::kv_import(int length, const float* key, const float* value, cudaStream_t s) {
+    if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    FB_RC(refuse());
+    if (!key || !value || length < 0 || length > capacity_) return FIRE_B200_ERR_INVALID;
+    const size_t row = size_t(kv_) * 4, part = size_t(length) * row;
+    for (int l = 0; l < d_.layers; ++l) {
+        const size_t dst = size_t(l) * capacity_ * kv_;
+        FB_CK(cudaMemcpyAsync(kcache_ + dst, reinterpret_cast<const char*>(key) + l * part, part, cudaMemcpyDefault, s));
+        FB_CK(cudaMemcpyAsync(vcache_ + dst, reinterpret_cast<const char*>(value) + l * part, part, cudaMemcpyDefault, s));
+    }
+    FB_CK(cudaStreamSynchronize(s));
+    length_ = length;
     return 0;
 }
 
@@ -865,6 +971,7 @@ int Qwen3Engine::prefill_chunk(int m, int mp, int pos0, cudaStream_t s) {
 
 int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaStream_t s) {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    FB_RC(refuse());
     if (tokens == nullptr || n <= 0 || length_ + n > capacity_) return FIRE_B200_ERR_INVALID;
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= d_.vocab) return FIRE_B200_ERR_INVALID;
@@ -920,18 +1027,21 @@ int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaSt
 
 int Qwen3Engine::generate(int first_token, int steps, int32_t* tokens_out, cudaStream_t s) {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    FB_RC(refuse());
     if (first_token < 0 || first_token >= d_.vocab || steps < 1) return FIRE_B200_ERR_INVALID;
     if (length_ + steps > capacity_) return FIRE_B200_ERR_STATE;
     FB_CK(set_state_launch(state_, first_token, length_, 0, s, false));
     for (int i = 0; i < steps; ++i) FB_RC(launch_step(s, true));
     if (tokens_out != nullptr && tokens_out != tokens_buf_)
         FB_CK(cudaMemcpyAsync(tokens_out, tokens_buf_, size_t(steps) * 4, cudaMemcpyDeviceToDevice, s));
+    FB_RC(mark_steps(s));
     length_ += steps;
     return 0;
 }
 
 int Qwen3Engine::generate_host(const int32_t* prompt, int n_prompt, int steps, int32_t* out_host, cudaStream_t s) {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    FB_RC(refuse());
     if (!prompt || n_prompt < 1 || steps < 1 || !out_host) return FIRE_B200_ERR_INVALID;
     if (length_ + n_prompt + steps - 1 > capacity_) return FIRE_B200_ERR_STATE;
     for (int i = 0; i < n_prompt; ++i)
@@ -947,9 +1057,12 @@ int Qwen3Engine::generate_host(const int32_t* prompt, int n_prompt, int steps, i
         *host_state_ = DecodeState{token, length_, 0, 0};
         FB_CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, s));
         FB_RC(launch_step(s, true));
-        FB_CK(cudaMemcpyAsync(host_token_, &state_->token, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-        FB_CK(cudaStreamSynchronize(s));
-        token = *host_token_;
+        // D2H of the state (sampled id and error word), then wait (with the host deadline
+        // under tensor parallelism)
+        FB_RC(mark_steps(s));
+        FB_RC(wait_event(steps_done_));
+        if (host_seen_->error != 0) return FIRE_B200_ERR_DEVICE;
+        token = host_seen_->token;
         out_host[i] = token;
         ++length_;  // the step consumed its input (n_prompt + steps - 1 tokens in all)
     }
@@ -965,6 +1078,13 @@ int Qwen3Engine::truncate(int length) {
 
 int Qwen3Engine::reset() {
     if (capacity_ == 0) return FIRE_B200_ERR_STATE;
+    if (aborted_) return FIRE_B200_ERR_TIMEOUT;
+    // a failed step leaves its error word in the state until here
+    FB_RC(wait_event(steps_done_));
+    FB_CK(cudaMemset(state_, 0, sizeof(DecodeState)));
+    if (stall_) FB_CK(cudaMemset(stall_, 0, sizeof(int)));  // an injected failure lasts until here
+    FB_CK(cudaDeviceSynchronize());
+    *host_seen_ = DecodeState{0, 0, 0, 0};
     length_ = 0;  // KVCache::reset (src/model/kv_cache.cpp:85)
     return 0;
 }

@@ -52,6 +52,7 @@ struct EngineOptions {
     const void* nccl_id = nullptr;  // 128-byte ncclUniqueId shared by all ranks (tp_size > 1)
     bool use_graph = true;
     bool pdl = true;
+    int deadline_ms = 0;  // host-side deadline of a synchronising wait under tensor parallelism (0 = 30 s)
 };
 
 struct W4Mat {
@@ -90,6 +91,19 @@ class Qwen3Engine {
     int prefill(const int32_t* tokens, int n, float* logits_out, cudaStream_t s);
     int reset();
     int truncate(int length);
+    // KVCache::key()/value() (include/Fire/model/kv_cache.h:24-28): copy positions
+    // [0, length) of every layer of this rank's cache shard to / from `key`, `value`
+    // ([layers][length][kv_heads/tp][128] FP32, host or device). Import sets the length.
+    // Both synchronise with `s`.
+    int kv_export(int length, float* key, float* value, cudaStream_t s) const;
+    int kv_import(int length, const float* key, const float* value, cudaStream_t s);
+    // Waits for the steps enqueued so far (under tensor parallelism with the host deadline,
+    // polling the communicator); FIRE_B200_ERR_DEVICE if a kernel recorded a failure in
+    // the decode state (its code in *device_error), FIRE_B200_ERR_TIMEOUT if the deadline
+    // ran out (the communicator is then aborted and the engine unusable).
+    int status(int* device_error);
+    // ncclCommAbort of this rank's communicator (tensor parallel); the engine is then dead
+    int abort();
 
     int length() const { return length_; }
     int capacity() const { return capacity_; }
@@ -120,8 +134,13 @@ class Qwen3Engine {
     int prefill_chunk(int m, int mp, int pos0, cudaStream_t s);
     int prefill_linear(const float* x, const uint8_t* items, int n, int k, float* y, int mp, cudaStream_t s);
     int capture(bool sample, cudaGraphExec_t* exec);
-    int capture_once(bool sample, cudaGraphExec_t* exec);
     int launch_step(cudaStream_t s, bool sample);
+    // after a group of steps: the state's error word to the pinned host mirror, and the
+    // event that status() waits for
+    int mark_steps(cudaStream_t s);
+    // FIRE_B200_ERR_DEVICE / _STATE when an earlier step failed or the engine was aborted
+    int refuse() const;
+    int wait_event(cudaEvent_t ev);
 
     Qwen3Dims d_;
     EngineOptions opt_;
@@ -161,7 +180,9 @@ class Qwen3Engine {
     void* best_all_ = nullptr;
     int32_t* tokens_buf_ = nullptr;
     DecodeState* host_state_ = nullptr;  // pinned, for generate_host
-    int32_t* host_token_ = nullptr;      // pinned
+    DecodeState* host_seen_ = nullptr;   // pinned: the device state copied back after each step group
+    cudaEvent_t steps_done_ = nullptr;   // recorded after that copy
+    bool aborted_ = false;               // the communicator was aborted at a deadline
     cudaGraphExec_t graph_fwd_ = nullptr, graph_step_ = nullptr;
     NcclComm comm_ = nullptr;
 
@@ -172,7 +193,6 @@ class Qwen3Engine {
     void* xchg_ = nullptr;
     void* xchg_peer_[kStackMaxTp] = {};
     int setup_exchange(std::string* err);
-    bool stack_coop_ = true;  // cooperative launch (falls back if the runtime refuses it)
     StackLayer* stack_layers_ = nullptr;  // device [layers]
     StackArgs stack_args_{};
     unsigned* stack_sync_ = nullptr;
@@ -187,6 +207,8 @@ class Qwen3Engine {
     void* pf_w_ = nullptr;  // BF16 copy of the matrix being multiplied
     int* pf_err_ = nullptr;
     bool stack_trace_on_ = false;  // FIRE_B200_STACK_TRACE=1: record the per-phase timeline
+    bool stall_on_ = false;        // FIRE_B200_FAULT_STALL=1 (tests): StackArgs::stall armed by prepare
+    int* stall_ = nullptr;         // device flag, cleared by reset()
     size_t stack_trace_words_ = 0;
 };
 

@@ -1127,7 +1127,8 @@ __device__ void attention_unit(const StackArgs& a, const Shared& sh, const Sched
 }
 
 template <int G, bool kTp>
-__device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos, unsigned tag_base) {
+__device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, int pos, unsigned tag_base,
+                         bool stall) {
     const int tid = threadIdx.x;
     unsigned seq = 0;
     for (int l = 0; l < a.L; ++l) {
@@ -1140,7 +1141,8 @@ __device__ void consumer(const StackArgs& a, const Shared& sh, const Sched& sc, 
             // input dependency: the phase before (layer 0's input comes from an earlier launch)
             if (l > 0 || p > 0) {
                 const int lp = p == 0 ? l - 1 : l, pp = p == 0 ? kStackPhases - 1 : p - 1;
-                wait_phase(a, sh, lp, pp, static_cast<unsigned>(min(sc.grid, sc.units(a, pp))));
+                const unsigned extra = stall && l == 0 && p == 2 ? 1u : 0u;  // failure injection
+                wait_phase(a, sh, lp, pp, static_cast<unsigned>(min(sc.grid, sc.units(a, pp))) + extra);
             } else {
                 cbar();
             }
@@ -1232,6 +1234,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs
         return;
     }
     const Sched sc = make_sched(a, pos);
+    const bool stall = a.stall != nullptr && *reinterpret_cast<const volatile int*>(a.stall) != 0;
     // tensor parallel: this launch's exchange tags (see StackArgs)
     const unsigned ep = kTp ? *reinterpret_cast<const volatile unsigned*>(a.epoch) : 0u;
     if (warp == W) {
@@ -1239,7 +1242,7 @@ __global__ void __launch_bounds__(kStackThreads, 1) stack_kernel(const StackArgs
     } else if (warp == W + 1) {
         prefetcher(a, sh, sc, pos);
     } else {
-        consumer<G, kTp>(a, sh, sc, pos, (ep + 1u) * static_cast<unsigned>(a.L + 1));
+        consumer<G, kTp>(a, sh, sc, pos, (ep + 1u) * static_cast<unsigned>(a.L + 1), stall);
         // every CTA read the epoch at its start, and CTA 0 gets here only after all ranks
         // finished the last layer
         if (kTp && blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.epoch) = ep + 1u;

@@ -110,6 +110,10 @@ struct StackArgs {
     // and warp 0's own progress: 10 scores done, 11 local softmax done, 12 P.V done;
     // GEMV phases: 7 warp 0's last item done (before the phase's finish step)
     unsigned long long* trace;
+    // failure injection for tests (nullptr in normal use): while *stall != 0, layer 0's o
+    // phase waits for one CTA more than the grid has, so that bounded wait runs out and
+    // the launch fails with kStackErrTimeout (a flag that nothing sets)
+    const int* stall;
     StackPhase ph[kStackPhases];  // index 1 (attention) unused
     // shared-memory plan (filled by stack_plan)
     int grid;

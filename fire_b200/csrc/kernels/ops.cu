@@ -260,13 +260,14 @@ __global__ void argmax_select_kernel(const ArgmaxPart* parts, int count, DecodeS
 }
 
 // Sets the decode control block from host values passed as kernel arguments, so a
-// host-driven step needs no host buffer that must outlive the launch.
+// host-driven step needs no host buffer that must outlive the launch. The error word is
+// left as it is: a failure recorded by an earlier step stays visible (and makes the
+// layer-stack kernel return at once) until the engine is reset.
 __global__ void set_state_kernel(DecodeState* state, int token, int pos, int step) {
     pdl_wait();
     state->token = token;
     state->pos = pos;
     state->step = step;
-    state->error = 0;
 }
 
 cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,

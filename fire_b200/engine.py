@@ -23,13 +23,13 @@ def _profile(p: Qwen3Profile) -> E.Profile:
                      p.num_attention_heads, p.num_kv_heads, p.head_dim, p.rms_norm_eps, p.rope_theta)
 
 
-def _options(tp_rank, tp_size, nccl_id, use_graph, pdl, keep) -> E.Options:
+def _options(tp_rank, tp_size, nccl_id, use_graph, pdl, deadline_ms, keep) -> E.Options:
     idp = None
     if nccl_id is not None:
         buf = C.create_string_buffer(bytes(nccl_id), 128)
         keep.append(buf)
         idp = C.cast(buf, C.c_void_p)
-    return E.Options(tp_rank, tp_size, idp, 1 if use_graph else 0, 1 if pdl else 0)
+    return E.Options(tp_rank, tp_size, idp, 1 if use_graph else 0, 1 if pdl else 0, int(deadline_ms))
 
 
 def _descriptor(name: str, a, keep) -> E.Tensor:
@@ -64,13 +64,13 @@ def nccl_unique_id() -> bytes:
 class Qwen3Engine:
     def __init__(self, profile: Qwen3Profile, tensors: Optional[Dict[str, object]] = None, *, path: str = None,
                  tp_rank: int = 0, tp_size: int = 1, nccl_id: Optional[bytes] = None, use_graph: bool = True,
-                 pdl: bool = True):
+                 pdl: bool = True, deadline_ms: int = 0):
         L = N.lib()
         self.profile = profile
         self.tp_rank, self.tp_size = tp_rank, tp_size
         keep: list = []
         prof = _profile(profile)
-        opts = _options(tp_rank, tp_size, nccl_id, use_graph, pdl, keep)
+        opts = _options(tp_rank, tp_size, nccl_id, use_graph, pdl, deadline_ms, keep)
         h = C.c_void_p()
         if path is not None:
             rc = L.fire_b200_qwen3_open(path.encode(), C.byref(prof), C.byref(opts), C.byref(h))
@@ -127,6 +127,39 @@ class Qwen3Engine:
     def truncate(self, length: int) -> None:
         N.check(self._L.fire_b200_qwen3_truncate(self._h, int(length)), "truncate")
 
+    def status(self) -> int:
+        """Waits for the enqueued steps; returns the device error code (0 = ok) or raises
+        FireB200Error(ERR_TIMEOUT) when the tensor-parallel deadline ran out."""
+        code = C.c_int(0)
+        rc = self._L.fire_b200_qwen3_status(self._h, C.byref(code))
+        if rc not in (N.OK, N.ERR_DEVICE):
+            raise N.FireB200Error(rc, "status")
+        return int(code.value)
+
+    def abort(self) -> None:
+        """Leave the tensor-parallel group (ncclCommAbort); the engine is then only fit for close()."""
+        N.check(self._L.fire_b200_qwen3_abort(self._h), "abort")
+
+    def kv_export(self, length: int):
+        """(key, value) numpy FP32 [layers, length, kv_heads_local, 128] of positions < length."""
+        p = self.profile
+        shape = (p.num_layers, int(length), p.num_kv_heads // self.tp_size, p.head_dim)
+        k, v = np.empty(shape, np.float32), np.empty(shape, np.float32)
+        N.check(self._L.fire_b200_qwen3_kv_export(self._h, int(length), k.ctypes.data, v.ctypes.data, None),
+                "kv_export")
+        return k, v
+
+    def kv_import(self, key, value) -> None:
+        """Load a KV prefix ([layers, length, kv_heads_local, 128] FP32) as the current sequence."""
+        k = np.ascontiguousarray(key, np.float32)
+        v = np.ascontiguousarray(value, np.float32)
+        p = self.profile
+        want = (p.num_layers, k.shape[1], p.num_kv_heads // self.tp_size, p.head_dim)
+        if k.shape != want or v.shape != want:
+            raise ValueError(f"KV prefix must be {want}")
+        N.check(self._L.fire_b200_qwen3_kv_import(self._h, int(k.shape[1]), k.ctypes.data, v.ctypes.data, None),
+                "kv_import")
+
     @property
     def length(self) -> int:
         return self._L.fire_b200_qwen3_length(self._h)
@@ -168,26 +201,3 @@ class Qwen3Engine:
     @property
     def step_weight_bytes(self) -> int:
         return int(self._L.fire_b200_qwen3_step_weight_bytes(self._h))
-
-
-def smoke_decode() -> None:
-    """Tiny Qwen3 on cuda:0: three forwards against the oracle, then a greedy check."""
-    import torch
-
-    from oracle import oracle as O
-
-    from . import synth
-    from .profiles import TINY
-
-    w = synth.generate(TINY, "int4", seed=1)
-    eng = Qwen3Engine(TINY, w)
-    eng.prepare(16)
-    ref = O.Qwen3Oracle(TINY, w, capacity=16)
-    logits = torch.empty(TINY.vocab_size, device="cuda")
-    for pos, tok in enumerate([3, 141, 592]):
-        eng.forward(tok, pos, logits)
-        torch.cuda.synchronize()
-        r = ref.forward(tok, pos)
-        rel = float(np.linalg.norm(logits.cpu().numpy() - r) / np.linalg.norm(r))
-        assert rel < 1e-4, f"engine logits rel-L2 {rel} at pos {pos}"
-    eng.close()

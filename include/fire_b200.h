@@ -38,7 +38,12 @@ enum {
     FIRE_B200_ERR_NO_DEVICE = -3,   /* no CUDA device / driver */
     FIRE_B200_ERR_STATE = -4,       /* engine used out of order (e.g. position mismatch) */
     FIRE_B200_ERR_IO = -5,          /* checkpoint file could not be read or is malformed */
-    FIRE_B200_ERR_NOMEM = -6        /* device memory reservation failed */
+    FIRE_B200_ERR_NOMEM = -6,       /* device memory reservation failed */
+    FIRE_B200_ERR_DEVICE = -7,      /* a kernel of an earlier step reported failure (a bounded
+                                       wait ran out, or it rejected the decode state); the
+                                       engine refuses steps until it is reset */
+    FIRE_B200_ERR_TIMEOUT = -8      /* a host-side deadline ran out (a tensor-parallel peer
+                                       stopped answering); the communicator was aborted */
 };
 
 /* Element types: dense weights and embedding tables (F32, BF16); packed INT4 and
@@ -122,17 +127,19 @@ int fire_b200_mha_decode(const float* q, const float* key_cache, const float* va
                          size_t workspace_bytes, void* stream);
 
 /* The same attention for callers that cannot allocate device memory or pass a workspace:
- * e.g. a plug-in behind an interface that hands over only its tensors (like Fire's
- * MHAKernel: q, caches, score, output), or a program whose device memory is fixed at
- * start-up so nothing may be allocated later. No counterpart in the reference: Fire's
- * kernel keeps its scores in the caller's `score` tensor and allocates nothing else.
- * Its scratch is a 4 MiB array inside the library (held in every GPU's memory from
- * library load to process exit), so it calls no allocator; shapes whose scratch,
+ * e.g. a plug-in behind an interface that hands it only the tensors it computes on (the
+ * query, the caches, the score buffer and the output; no scratch argument), or a program
+ * whose device memory is fixed at start-up so nothing may be allocated later. This entry
+ * point has no counterpart in the reference. Its scratch is a 4 MiB array inside the
+ * library (held in every GPU's memory from library load to process exit), so it calls no
+ * allocator; shapes whose scratch,
  * fire_b200_mha_workspace_bytes(q_heads, kv_heads, head_dim, capacity), exceeds
  * 4 MiB are rejected with FIRE_B200_ERR_UNSUPPORTED (e.g. 32 q heads of dim 128 fit up
  * to capacity 16128). The first call on each device looks the array's device address
- * up (make that first call before any stream capture). All calls share the array:
- * calls that overlap on the GPU race and must be serialised by the caller. */
+ * up (make that first call before any stream capture); the address is kept for the life
+ * of the process, so after a cudaDeviceReset this entry point must not be called again
+ * on that device. All calls share the array: calls that overlap on the GPU race and must
+ * be serialised by the caller. */
 int fire_b200_mha_decode_noalloc(const float* q, const float* key_cache, const float* value_cache,
                                  float* score, float* out, int layers, int capacity, int q_heads,
                                  int kv_heads, int head_dim, int layer, int pos, void* stream);

@@ -46,6 +46,8 @@ typedef struct {
     const void* nccl_id;  /* 128-byte NCCL unique id, the same on every rank (tp_size > 1) */
     int use_graph;        /* capture each decode step in a CUDA graph (recommended: 1) */
     int pdl;              /* programmatic dependent launch between kernels (recommended: 1) */
+    int deadline_ms;      /* tensor parallel: host-side deadline of a synchronising wait
+                             (generate_host, status, reset); 0 = 30000 */
 } fire_b200_qwen3_options;
 
 /* A new NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */
@@ -78,8 +80,35 @@ int fire_b200_qwen3_generate(fire_b200_qwen3* m, int first_token, int steps, int
  * the sampled id and a stream synchronisation. prompt/out are host arrays; out gets `steps` ids. */
 int fire_b200_qwen3_generate_host(fire_b200_qwen3* m, const int32_t* prompt, int n_prompt, int steps,
                                   int32_t* out, void* stream);
-/* Model::reset: empty the sequence, keep weights and capacity. */
+/* Model::reset: empty the sequence, keep weights and capacity. Also clears a failure
+ * recorded by an earlier step (see fire_b200_qwen3_status). */
 int fire_b200_qwen3_reset(fire_b200_qwen3* m);
+/* Outcome of the steps enqueued so far. Launches are asynchronous ("CUDA success means
+ * submission", include/Fire/model/model.h:41-42), so a kernel that fails a step records a
+ * code in the engine's device-side decode state instead: 1 position rejected, 2 token
+ * rejected, 3 a bounded wait of the layer-stack kernel ran out (a peer or a CTA that never
+ * arrived). This call waits for the last step and returns FIRE_B200_OK, or
+ * FIRE_B200_ERR_DEVICE with the code in *device_error (if not NULL). After a failure every
+ * step entry point returns FIRE_B200_ERR_DEVICE until fire_b200_qwen3_reset. Under tensor
+ * parallelism the wait has the host deadline of the options; when it runs out, or NCCL
+ * reports an asynchronous error, the communicator is aborted (ncclCommAbort) and the call
+ * returns FIRE_B200_ERR_TIMEOUT; the engine is then only fit for destroy. */
+int fire_b200_qwen3_status(fire_b200_qwen3* m, int* device_error);
+/* Leave a tensor-parallel group without waiting for the peers: abort this rank's NCCL
+ * communicator (ncclCommAbort ends its kernels in flight). No reference counterpart (Fire
+ * is single-device). The engine then returns FIRE_B200_ERR_TIMEOUT from every step and is
+ * only fit for destroy. A no-op at tp_size 1. */
+int fire_b200_qwen3_abort(fire_b200_qwen3* m);
+/* KVCache::key() / value() (include/Fire/model/kv_cache.h:24-28): copy the FP32 K and V
+ * of positions [0, length) of every layer out of the engine. `key` and `value` are
+ * [num_layers][length][kv_heads_local][head_dim], kv_heads_local = num_kv_heads / tp_size
+ * (this rank's heads), host or device memory; length <= fire_b200_qwen3_length.
+ * Synchronises with `stream`. */
+int fire_b200_qwen3_kv_export(const fire_b200_qwen3* m, int length, float* key, float* value, void* stream);
+/* The reverse: load a KV prefix of `length` positions (same layout) and make it the current
+ * sequence, as if those tokens had been consumed (a saved prompt, or a prefix shared with a
+ * checker). Synchronises with `stream`. */
+int fire_b200_qwen3_kv_import(fire_b200_qwen3* m, int length, const float* key, const float* value, void* stream);
 /* Shorten the sequence to `length` tokens (0 <= length <= current length), keeping the KV
  * cache of the kept prefix, so a shared prompt can be decoded from again. */
 int fire_b200_qwen3_truncate(fire_b200_qwen3* m, int length);

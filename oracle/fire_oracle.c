@@ -55,8 +55,240 @@ void fo_dequant_int4(const uint8_t* qw, const float* scales, const uint8_t* zero
     }
 }
 
+/* Row-blocked forms. Each output row keeps the reference's sequential accumulation
+ * order over k (sum = sum + x[k]*w[k], one rounding per operation); eight rows advance in
+ * lock step in the lanes of one vector, so the results are bit-identical to the one-row
+ * loops (the *_scalar functions below, kept for the test that checks exactly that). */
+typedef float fo_v8 __attribute__((vector_size(32)));
+enum { FO_RB = 8, FO_CB = 256 };
+
+/* one block of up to 8 rows: tile[j][r] holds w[r0 + r][c0 + j] for a chunk of columns */
+typedef void (*fo_fill_fn)(const void* ctx, int64_t r0, int nr, int64_t c0, int cn, fo_v8* tile);
+
+static void fo_rows8(const float* xr, const void* ctx, fo_fill_fn fill, float scale, float* y,
+                     int64_t r0, int nr, int64_t k) {
+    fo_v8 tile[FO_CB];
+    fo_v8 acc = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t c0 = 0; c0 < k; c0 += FO_CB) {
+        const int cn = (int)((k - c0) < FO_CB ? (k - c0) : FO_CB);
+        fill(ctx, r0, nr, c0, cn, tile);
+        for (int j = 0; j < cn; ++j) {
+            const fo_v8 xv = {xr[c0 + j], xr[c0 + j], xr[c0 + j], xr[c0 + j],
+                              xr[c0 + j], xr[c0 + j], xr[c0 + j], xr[c0 + j]};
+            acc = acc + xv * tile[j];
+        }
+    }
+    for (int r = 0; r < nr; ++r) y[r0 + r] = scale == 1.0f ? acc[r] : acc[r] * scale;
+}
+
+static void fo_blocked(const float* x, const void* ctx, fo_fill_fn fill, float scale, float* y,
+                       int64_t m, int64_t n, int64_t k) {
+    const int64_t blocks = (n + FO_RB - 1) / FO_RB;
+    for (int64_t row = 0; row < m; ++row) {
+        const float* xr = x + row * k;
+        float* yr = y + row * n;
+#pragma omp parallel for schedule(static) num_threads(fo_get_threads())
+        for (int64_t b = 0; b < blocks; ++b) {
+            const int64_t r0 = b * FO_RB;
+            const int nr = (int)((n - r0) < FO_RB ? (n - r0) : FO_RB);
+            fo_rows8(xr, ctx, fill, scale, yr, r0, nr, k);
+        }
+    }
+}
+
+typedef struct { const float* w; int64_t k; } fo_f32_ctx;
+static void fill_f32(const void* p, int64_t r0, int nr, int64_t c0, int cn, fo_v8* tile) {
+    const fo_f32_ctx* c = (const fo_f32_ctx*)p;
+    for (int r = 0; r < FO_RB; ++r) {
+        const float* wr = c->w + (r0 + (r < nr ? r : 0)) * c->k + c0;
+        for (int j = 0; j < cn; ++j) tile[j][r] = r < nr ? wr[j] : 0.0f;
+    }
+}
+
+typedef struct { const uint16_t* w; int64_t k; } fo_bf16_ctx;
+static void fill_bf16(const void* p, int64_t r0, int nr, int64_t c0, int cn, fo_v8* tile) {
+    const fo_bf16_ctx* c = (const fo_bf16_ctx*)p;
+    for (int r = 0; r < FO_RB; ++r) {
+        const uint16_t* wr = c->w + (r0 + (r < nr ? r : 0)) * c->k + c0;
+        for (int j = 0; j < cn; ++j) tile[j][r] = r < nr ? fo_bf16_to_f32(wr[j]) : 0.0f;
+    }
+}
+
+typedef struct { const uint8_t* qw; const float* s; const uint8_t* z; int64_t k; int group; } fo_w4_ctx;
+/* tools/quant.py:227-255 per element: s * (float(q) - float(z)), even k in the low nibble */
+static void fill_w4(const void* p, int64_t r0, int nr, int64_t c0, int cn, fo_v8* tile) {
+    const fo_w4_ctx* c = (const fo_w4_ctx*)p;
+    const int64_t groups = c->k / c->group;
+    for (int r = 0; r < FO_RB; ++r) {
+        if (r >= nr) {
+            for (int j = 0; j < cn; ++j) tile[j][r] = 0.0f;
+            continue;
+        }
+        const uint8_t* qrow = c->qw + (r0 + r) * (c->k / 2);
+        const float* srow = c->s + (r0 + r) * groups;
+        const uint8_t* zrow = c->z + (r0 + r) * groups;
+        int64_t g = c0 / c->group, gend = (g + 1) * c->group;
+        float s = srow[g], zf = (float)zrow[g];
+        for (int j = 0; j < cn; ++j) {
+            const int64_t col = c0 + j;
+            if (col == gend) {
+                ++g;
+                gend += c->group;
+                s = srow[g];
+                zf = (float)zrow[g];
+            }
+            const uint8_t b = qrow[col >> 1];
+            const int q = (col & 1) ? (b >> 4) : (b & 15);
+            tile[j][r] = s * ((float)q - zf);
+        }
+    }
+}
+
+/* Fast forms for the decode shapes: eight rows per vector, eight columns per step. A
+ * 32-bit word of each row holds its next eight nibbles (INT4) or two BF16 values, so every
+ * column becomes a lane-wise shift / mask / convert, with the same per-element arithmetic
+ * and the same per-row order as above. Compiled twice: AVX2 when the host has it, else
+ * the baseline vector code (identical results either way: no FMA, one rounding per op). */
+typedef uint32_t fo_v8u __attribute__((vector_size(32)));
+typedef int32_t fo_v8i __attribute__((vector_size(32)));
+
+static inline uint32_t fo_ld32(const void* p) {
+    uint32_t v;
+    memcpy(&v, p, 4);
+    return v;
+}
+
+#define FO_W4_BODY                                                                              \
+    const int64_t groups = k / group;                                                           \
+    fo_v8 acc = {0, 0, 0, 0, 0, 0, 0, 0};                                                       \
+    const uint8_t* q[FO_RB];                                                                    \
+    for (int r = 0; r < FO_RB; ++r) q[r] = qw + (r0 + (r < nr ? r : 0)) * (k / 2);               \
+    for (int64_t g = 0; g < groups; ++g) {                                                      \
+        fo_v8 s, zf;                                                                            \
+        for (int r = 0; r < FO_RB; ++r) {                                                       \
+            const int64_t rr = r0 + (r < nr ? r : 0);                                           \
+            s[r] = scales[rr * groups + g];                                                     \
+            zf[r] = (float)zeros[rr * groups + g];                                              \
+        }                                                                                       \
+        for (int64_t c = g * group; c < (g + 1) * group; c += 8) {                              \
+            fo_v8u wv;                                                                          \
+            for (int r = 0; r < FO_RB; ++r) wv[r] = fo_ld32(q[r] + (c >> 1));                   \
+            for (int j = 0; j < 8; ++j) {                                                       \
+                const fo_v8i qi = (fo_v8i)((wv >> (4u * (unsigned)j)) & 15u);                  \
+                const fo_v8 w = s * (__builtin_convertvector(qi, fo_v8) - zf);                  \
+                const float xs = xr[c + j];                                                     \
+                const fo_v8 xv = {xs, xs, xs, xs, xs, xs, xs, xs};                              \
+                acc = acc + xv * w;                                                             \
+            }                                                                                   \
+        }                                                                                       \
+    }                                                                                           \
+    for (int r = 0; r < nr; ++r) y[r0 + r] = acc[r];
+
+#define FO_BF16_BODY                                                                            \
+    fo_v8 acc = {0, 0, 0, 0, 0, 0, 0, 0};                                                       \
+    const uint16_t* wp[FO_RB];                                                                  \
+    for (int r = 0; r < FO_RB; ++r) wp[r] = w + (r0 + (r < nr ? r : 0)) * k;                     \
+    for (int64_t c = 0; c < k; c += 2) {                                                        \
+        fo_v8u wv;                                                                              \
+        for (int r = 0; r < FO_RB; ++r) wv[r] = fo_ld32(wp[r] + c);                             \
+        const fo_v8u lo = wv << 16u, hi = wv & 0xFFFF0000u;                                     \
+        fo_v8 w0, w1;                                                                           \
+        memcpy(&w0, &lo, sizeof w0);                                                            \
+        memcpy(&w1, &hi, sizeof w1);                                                            \
+        const fo_v8 x0 = {xr[c], xr[c], xr[c], xr[c], xr[c], xr[c], xr[c], xr[c]};              \
+        const fo_v8 x1 = {xr[c + 1], xr[c + 1], xr[c + 1], xr[c + 1],                           \
+                          xr[c + 1], xr[c + 1], xr[c + 1], xr[c + 1]};                          \
+        acc = acc + x0 * w0;                                                                    \
+        acc = acc + x1 * w1;                                                                    \
+    }                                                                                           \
+    for (int r = 0; r < nr; ++r) y[r0 + r] = acc[r] * scale;
+
+__attribute__((target("avx2"))) static void w4_rows8_avx2(const float* xr, const uint8_t* qw,
+                                                          const float* scales,
+                                                          const uint8_t* zeros, float* y,
+                                                          int64_t r0, int nr, int64_t k,
+                                                          int group) {
+    FO_W4_BODY
+}
+static void w4_rows8_base(const float* xr, const uint8_t* qw, const float* scales,
+                          const uint8_t* zeros, float* y, int64_t r0, int nr, int64_t k,
+                          int group) {
+    FO_W4_BODY
+}
+__attribute__((target("avx2"))) static void bf16_rows8_avx2(const float* xr, const uint16_t* w,
+                                                            float scale, float* y, int64_t r0,
+                                                            int nr, int64_t k) {
+    FO_BF16_BODY
+}
+static void bf16_rows8_base(const float* xr, const uint16_t* w, float scale, float* y,
+                            int64_t r0, int nr, int64_t k) {
+    FO_BF16_BODY
+}
+
+static int fo_avx2(void) {
+    static int v = -1;
+    if (v < 0) v = __builtin_cpu_supports("avx2") ? 1 : 0;
+    return v;
+}
+
 void fo_linear_f32(const float* x, const float* w, float scale, float* y, int64_t m, int64_t n,
                    int64_t k) {
+    const fo_f32_ctx c = {w, k};
+    fo_blocked(x, &c, fill_f32, scale, y, m, n, k);
+}
+
+void fo_linear_bf16(const float* x, const uint16_t* w, float scale, float* y, int64_t m,
+                    int64_t n, int64_t k) {
+    if (k % 2) {
+        const fo_bf16_ctx c = {w, k};
+        fo_blocked(x, &c, fill_bf16, scale, y, m, n, k);
+        return;
+    }
+    const int avx2 = fo_avx2();
+    const int64_t blocks = (n + FO_RB - 1) / FO_RB;
+    for (int64_t row = 0; row < m; ++row) {
+        const float* xr = x + row * k;
+        float* yr = y + row * n;
+#pragma omp parallel for schedule(static) num_threads(fo_get_threads())
+        for (int64_t b = 0; b < blocks; ++b) {
+            const int64_t r0 = b * FO_RB;
+            const int nr = (int)((n - r0) < FO_RB ? (n - r0) : FO_RB);
+            if (avx2)
+                bf16_rows8_avx2(xr, w, scale, yr, r0, nr, k);
+            else
+                bf16_rows8_base(xr, w, scale, yr, r0, nr, k);
+        }
+    }
+}
+
+void fo_linear_int4(const float* x, const uint8_t* qw, const float* scales,
+                    const uint8_t* zeros, float* y, int64_t m, int64_t n, int64_t k, int group) {
+    if (group % 8 || k % 8) {
+        const fo_w4_ctx c = {qw, scales, zeros, k, group};
+        fo_blocked(x, &c, fill_w4, 1.0f, y, m, n, k);
+        return;
+    }
+    const int avx2 = fo_avx2();
+    const int64_t blocks = (n + FO_RB - 1) / FO_RB;
+    for (int64_t row = 0; row < m; ++row) {
+        const float* xr = x + row * k;
+        float* yr = y + row * n;
+#pragma omp parallel for schedule(static) num_threads(fo_get_threads())
+        for (int64_t b = 0; b < blocks; ++b) {
+            const int64_t r0 = b * FO_RB;
+            const int nr = (int)((n - r0) < FO_RB ? (n - r0) : FO_RB);
+            if (avx2)
+                w4_rows8_avx2(xr, qw, scales, zeros, yr, r0, nr, k, group);
+            else
+                w4_rows8_base(xr, qw, scales, zeros, yr, r0, nr, k, group);
+        }
+    }
+}
+
+/* One row at a time, exactly as the reference CPU kernels loop (the yardstick the
+ * row-blocked forms above are checked against, bit for bit). */
+void fo_linear_f32_scalar(const float* x, const float* w, float scale, float* y, int64_t m,
+                          int64_t n, int64_t k) {
     for (int64_t row = 0; row < m; ++row) {
         const float* xr = x + row * k;
 #pragma omp parallel for schedule(static) num_threads(fo_get_threads())
@@ -69,8 +301,8 @@ void fo_linear_f32(const float* x, const float* w, float scale, float* y, int64_
     }
 }
 
-void fo_linear_bf16(const float* x, const uint16_t* w, float scale, float* y, int64_t m,
-                    int64_t n, int64_t k) {
+void fo_linear_bf16_scalar(const float* x, const uint16_t* w, float scale, float* y, int64_t m,
+                           int64_t n, int64_t k) {
     for (int64_t row = 0; row < m; ++row) {
         const float* xr = x + row * k;
 #pragma omp parallel for schedule(static) num_threads(fo_get_threads())
@@ -83,8 +315,9 @@ void fo_linear_bf16(const float* x, const uint16_t* w, float scale, float* y, in
     }
 }
 
-void fo_linear_int4(const float* x, const uint8_t* qw, const float* scales,
-                    const uint8_t* zeros, float* y, int64_t m, int64_t n, int64_t k, int group) {
+void fo_linear_int4_scalar(const float* x, const uint8_t* qw, const float* scales,
+                           const uint8_t* zeros, float* y, int64_t m, int64_t n, int64_t k,
+                           int group) {
     const int64_t groups = k / group;
     for (int64_t row = 0; row < m; ++row) {
         const float* xr = x + row * k;
@@ -190,6 +423,8 @@ void fo_mha(const float* q, const float* key_cache, const float* value_cache, fl
     const int kv_mul = q_heads / kv_heads;
     const float scale = 1.0f / sqrtf((float)head_dim);
     const int64_t layer_off = (int64_t)layer * capacity * kv_heads * head_dim;
+    /* heads are independent: one thread per head, each head's loops unchanged */
+#pragma omp parallel for schedule(static) num_threads(fo_get_threads())
     for (int h = 0; h < q_heads; ++h) {
         float* sh = score + (int64_t)h * capacity;
         const float* qh = q + (int64_t)h * head_dim;

@@ -46,6 +46,16 @@ void fo_linear_bf16(const float* x, const uint16_t* w, float scale, float* y, in
  * Any group size dividing k, k even. */
 void fo_linear_int4(const float* x, const uint8_t* qw, const float* scales,
                     const uint8_t* zeros, float* y, int64_t m, int64_t n, int64_t k, int group);
+/* The three linears above compute eight rows in lock step (vector lanes), each row in the
+ * reference's sequential order; these one-row-at-a-time forms are the plain loops they must
+ * equal bit for bit. */
+void fo_linear_f32_scalar(const float* x, const float* w, float scale, float* y, int64_t m,
+                          int64_t n, int64_t k);
+void fo_linear_bf16_scalar(const float* x, const uint16_t* w, float scale, float* y, int64_t m,
+                           int64_t n, int64_t k);
+void fo_linear_int4_scalar(const float* x, const uint8_t* qw, const float* scales,
+                           const uint8_t* zeros, float* y, int64_t m, int64_t n, int64_t k,
+                           int group);
 /* Same products accumulated in double: the error yardstick for tolerance tests. */
 void fo_linear_int4_f64(const float* x, const uint8_t* qw, const float* scales,
                         const uint8_t* zeros, double* y, int64_t m, int64_t n, int64_t k,

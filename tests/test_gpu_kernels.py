@@ -75,6 +75,44 @@ def test_w4_decode_shapes_vs_oracle(cuda, n, k):
     assert rel_l2(got, O.linear_int4_f64(x, qw, s, z)) <= REL_L2
 
 
+def config3_w4(n, k, seed):
+    """Qwen3-8B mixed-layout GEMV weights: W ~ N(0, 0.02) from default_rng(seed), RTN INT4
+    group 128 by the reference rule (tools/quant.py:14-137), scales rounded to FP16 values
+    (stored FP32), 4-bit zero points; x ~ N(0, 1) drawn after W."""
+    rng = np.random.default_rng(seed)
+    W = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+    x = rng.normal(0, 1, k).astype(np.float32)
+    q, s, z = quant.quantize_int4_groupwise(W, 128)
+    return x, quant.pack_uint4(q), s.astype(np.float16).astype(np.float32), z
+
+
+@pytest.mark.parametrize("name,n,k", [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096), ("o", 4096, 4096),
+                                      ("gate", 12288, 4096), ("up", 12288, 4096), ("down", 4096, 12288)])
+def test_w4_qwen3_8b_gemv_sweep_shapes_rtn(cuda, name, n, k):
+    """Every Qwen3-8B projection at M=1 on RTN weights with FP16-valued scales, against the
+    oracle's dequantise-then-FP32 Linear and its float64 sum (rel-L2 <= 1e-5 each)."""
+    x, qw, s, z = config3_w4(n, k, seed=0)
+    y = torch.empty(n, device="cuda")
+    assert w4(dev(x), dev(qw), dev(s), dev(z), y, 1, n, k, 128) == N.OK
+    got = host(y)
+    assert rel_l2(got, O.linear_int4(x, qw, s, z)) <= REL_L2
+    assert rel_l2(got, O.linear_int4_f64(x, qw, s, z)) <= REL_L2
+
+
+def test_bf16_head_qwen3_8b_rtn_workload(cuda):
+    """The BF16 LM head of the sweep: W [151936, 4096] ~ N(0, 0.02) rounded to BF16, x ~ N(0, 1)."""
+    n, k = 151936, 4096
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(k, device="cuda", generator=g)
+    y = torch.empty(n, device="cuda")
+    rc = N.lib().fire_b200_linear_dense(x.data_ptr(), w.data_ptr(), N.BF16, 1.0, y.data_ptr(), 1, n, k, 0)
+    assert rc == N.OK
+    ref = O.linear_bf16(host(x), host(w.view(torch.int16)).view(np.uint16))
+    assert rel_l2(host(y), ref) <= REL_L2
+
+
 @pytest.mark.skipif(not O.ref_available(), reason="reference kernels not built (oracle/_ref)")
 @pytest.mark.parametrize("n,k", [(4096, 4096), (1024, 4096), (12288, 4096), (4096, 12288), (3072, 1024)])
 def test_w4_matches_reference_cuda_gemv(cuda, n, k):

@@ -192,3 +192,40 @@ def test_oracle_qwen3_forward_runs_and_resets():
     assert all(np.array_equal(x, y) for x, y in zip(a, b))
     with pytest.raises(ValueError):
         m.forward(1, 7)
+
+
+@pytest.mark.parametrize("n,k,group", [(7, 258, 3), (19, 256, 128), (33, 1024, 128), (13, 132, 4),
+                                       (1027, 4096, 128), (9, 12288, 128)])
+def test_oracle_row_blocked_int4_equals_one_row_loops(n, k, group):
+    """The oracle's INT4 Linear runs eight rows in vector lanes; each row must still sum in
+    the reference's sequential order, so it equals the one-row loop bit for bit."""
+    import ctypes as C
+    rng = np.random.default_rng(n + k)
+    q = rng.integers(0, 256, (n, k // 2), dtype=np.uint8)
+    s = rng.random((n, k // group), dtype=np.float32) * 0.02
+    z = rng.integers(0, 16, (n, k // group), dtype=np.uint8)
+    x = rng.standard_normal((2, k), dtype=np.float32)
+    L = O.lib()
+    L.fo_linear_int4_scalar.argtypes = [O._f32p, O._u8p, O._f32p, O._u8p, O._f32p, C.c_int64, C.c_int64,
+                                        C.c_int64, C.c_int]
+    want = np.empty((2, n), np.float32)
+    L.fo_linear_int4_scalar(x, q, s, z, want, 2, n, k, group)
+    got = O.linear_int4(x, q, s, z, group)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,k", [(33, 37), (1000, 4096), (17, 2)])
+def test_oracle_row_blocked_dense_equals_one_row_loops(n, k):
+    import ctypes as C
+    rng = np.random.default_rng(n * k)
+    x = rng.standard_normal((1, k), dtype=np.float32)
+    wf = rng.standard_normal((n, k), dtype=np.float32)
+    wb = (wf.view(np.uint32) >> 16).astype(np.uint16)
+    L = O.lib()
+    L.fo_linear_bf16_scalar.argtypes = [O._f32p, O._u16p, C.c_float, O._f32p, C.c_int64, C.c_int64, C.c_int64]
+    L.fo_linear_f32_scalar.argtypes = [O._f32p, O._f32p, C.c_float, O._f32p, C.c_int64, C.c_int64, C.c_int64]
+    want = np.empty((1, n), np.float32)
+    L.fo_linear_bf16_scalar(x, wb, 1.0, want, 1, n, k)
+    assert np.array_equal(O.linear_bf16(x, wb).view(np.uint32), want.view(np.uint32))
+    L.fo_linear_f32_scalar(x, wf, 0.5, want, 1, n, k)
+    assert np.array_equal(O.linear_f32(x, wf, 0.5).view(np.uint32), want.view(np.uint32))
