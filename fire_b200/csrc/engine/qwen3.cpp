@@ -249,6 +249,13 @@ int Qwen3Engine::import_weights(const std::vector<TensorSrc>& tensors, std::stri
     FB_RC(weight_arena_->reserve(total + 4096));
     weight_bytes_ = total;
 
+    // Device-resident sources may still be in the making on the caller's streams (e.g. a
+    // framework's kernels that filled them, queued on its own stream). The copies below run
+    // on a private non-blocking stream, which is not ordered after any of those, so wait for
+    // the device first.
+    bool any_device = false;
+    for (const auto& t : tensors) any_device = any_device || t.on_device;
+    if (any_device) FB_CK(cudaDeviceSynchronize());
     cudaStream_t s;
     FB_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
     auto alloc = [&](size_t b) { return weight_arena_->alloc(b); };

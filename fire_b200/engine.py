@@ -76,6 +76,10 @@ class Qwen3Engine:
             rc = L.fire_b200_qwen3_open(path.encode(), C.byref(prof), C.byref(opts), C.byref(h))
         else:
             descs = [_descriptor(n, a, keep) for n, a in tensors.items()]
+            if any(d.on_device for d in descs):
+                import torch
+
+                torch.cuda.synchronize()  # the engine copies on its own stream
             arr = (E.Tensor * len(descs))(*descs)
             rc = L.fire_b200_qwen3_create(C.byref(prof), arr, len(descs), C.byref(opts), C.byref(h))
         if rc != N.OK:

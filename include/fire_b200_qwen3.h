@@ -55,7 +55,9 @@ int fire_b200_nccl_unique_id(void* id128);
 
 /* Import weights (INT4 group-128 projections; FP32/BF16/INT4 LM head; FP32/BF16
  * embedding) into device memory and build the engine: Qwen3Loader::load_weights +
- * Qwen3Model::create. Tensor parallel ranks keep only their shard. */
+ * Qwen3Model::create. Tensor parallel ranks keep only their shard. When any tensor is in
+ * device memory the call first synchronises the device, so tensors still being written by
+ * work queued on other streams are read complete. */
 int fire_b200_qwen3_create(const fire_b200_qwen3_profile* profile, const fire_b200_tensor* tensors, int count,
                            const fire_b200_qwen3_options* options, fire_b200_qwen3** out);
 /* The same from a .fire v1/v2 file (Qwen3Loader::open, src/model/qwen_loader.cpp:12-17). */

@@ -171,3 +171,38 @@ def test_qwen3_0_6b_greedy_256_steps_identical_to_oracle(cuda):
             lg = ref.forward(nxt, len(prompt) + i)
     mismatch = [i for i in range(256) if got[i] != want[i]]
     assert not mismatch, f"first mismatch at step {mismatch[0]}, top-2 margin {margins[mismatch[0]]:.3e}"
+
+
+def test_engine_reads_device_weights_still_being_written(cuda):
+    """Weights made on the GPU by work still queued on another stream (as a framework does)
+    must be read complete: the engine waits for the device before importing them."""
+    p = SMALL
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        torch.cuda._sleep(50_000_000)  # keep the stream busy so the weights land late
+        w = synth.generate_torch(p, "mixed", seed=6, device="cuda")
+    # straight through the C ABI (the Python wrapper would synchronise first)
+    import ctypes as C
+
+    from fire_b200 import _engine_sigs as E
+    from fire_b200 import engine as EM
+
+    keep = []
+    descs = [EM._descriptor(n, a, keep) for n, a in w.items()]
+    arr = (E.Tensor * len(descs))(*descs)
+    h = C.c_void_p()
+    L = N.lib()
+    rc = L.fire_b200_qwen3_create(C.byref(EM._profile(p)), arr, len(descs),
+                                  C.byref(EM._options(0, 1, None, True, True, 0, keep)), C.byref(h))
+    assert rc == N.OK
+    eng = Qwen3Engine.__new__(Qwen3Engine)
+    eng.profile, eng.tp_rank, eng.tp_size, eng._h, eng._L = p, 0, 1, h, L
+    side.synchronize()
+    wn = {k: (v.cpu().numpy().view(np.uint16) if v.dtype == torch.int16 else v.cpu().numpy()) for k, v in w.items()}
+    eng.prepare(8)
+    ref = O.Qwen3Oracle(p, wn, capacity=8)
+    logits = torch.empty(p.vocab_size, device="cuda")
+    for pos, t in enumerate([5, 77]):
+        eng.forward(t, pos, logits)
+        torch.cuda.synchronize()
+        check_logits(logits.cpu().numpy(), ref.forward(t, pos))
