@@ -49,7 +49,15 @@ SIGNATURES: Dict[str, tuple] = {
     "fire_b200_add": (_i, [_vp, _vp, _vp, _i, _vp]),
     "fire_b200_argmax_workspace_bytes": (_sz, []),
     "fire_b200_argmax": (_i, [_vp, _i64, _vp, _vp, _sz, _vp]),
+    # include/fire_b200_alloc.h
+    "fire_b200_device_alloc": (_i, [_sz, C.POINTER(_vp)]),
+    "fire_b200_device_release": (_i, [_vp]),
+    "fire_b200_device_memset_zero": (_i, [_vp, _sz, _vp, _i]),
+    "fire_b200_device_memcpy": (_i, [_vp, _vp, _sz, _i, _vp, _i]),
+    "fire_b200_device_pool_stats": (_i, [_i, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz)]),
+    "fire_b200_device_pool_trim": (_i, [_i]),
 }
+CPU2GPU, CPU2CPU, GPU2CPU, GPU2GPU = 0, 1, 2, 3
 
 
 def declared_symbols() -> List[str]:
