@@ -716,7 +716,8 @@ def run_ours(args):
             line["single_linear"] = lin
         line["prefill"] = {"prompt_tokens": n_prompt - 1, "ms": round(prefill_ms, 2),
                            "tok_s": round((n_prompt - 1) / (prefill_ms / 1e3), 1) if prefill_ms > 0 else None,
-                           "path": "batched tcgen05 prefill" if world == 1 else "forward() per token",
+                           "path": "batched tcgen05 prefill" + (f" (tensor parallel over {world}, o/down "
+                                                                 f"all-reduced)" if world > 1 else ""),
                            "note": "host wall clock around fire_b200_qwen3_prefill (synchronising)"}
         if world == 1:
             line["prefill_gemm"] = prefill_sweep()

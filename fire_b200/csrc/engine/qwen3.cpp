@@ -963,14 +963,19 @@ int Qwen3Engine::prefill_chunk(int m, int mp, int pos0, cudaStream_t s) {
         pa.attn_out = pf_att_;
         FB_CK(qk_rope_kv_rows_launch(pa, s));
         FB_CK(causal_attention_launch(pa, s));
-        // o projection + residual (qwen.cpp:249-262)
+        // o projection + residual (qwen.cpp:249-262); under tensor parallelism each rank holds
+        // a K slice of o (its heads), so the rows are partial sums: all-reduced first
         FB_RC(prefill_linear(pf_att_, L.o_items, H, q_, pf_o_, mp, s));
+        if (tp_ > 1 && nccl().AllReduce(pf_o_, pf_o_, size_t(mp) * H, kNcclFloat32, 0, comm_, s) != 0)
+            return FIRE_B200_ERR_STATE;
         FB_CK(add_launch(pf_x_, pf_o_, pf_x_, mp * H, sms_, s));
         // SwiGLU FFN + residual (qwen.cpp:264-291)
         FB_CK(rmsnorm_rows_launch(pf_x_, L.ffn_norm, pf_xn_, mp, H, d_.eps, s));
         FB_RC(prefill_linear(pf_xn_, L.gu_items, 2 * f_, H, pf_gu_, mp, s));
         FB_CK(swiglu_packed_rows_launch(pf_gu_, pf_act_, mp, f_, sms_, s));
         FB_RC(prefill_linear(pf_act_, L.down_items, H, f_, pf_o_, mp, s));
+        if (tp_ > 1 && nccl().AllReduce(pf_o_, pf_o_, size_t(mp) * H, kNcclFloat32, 0, comm_, s) != 0)
+            return FIRE_B200_ERR_STATE;
         FB_CK(add_launch(pf_x_, pf_o_, pf_x_, mp * H, sms_, s));
     }
     return 0;
@@ -982,7 +987,7 @@ int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaSt
     if (tokens == nullptr || n <= 0 || length_ + n > capacity_) return FIRE_B200_ERR_INVALID;
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= d_.vocab) return FIRE_B200_ERR_INVALID;
-    if (!stack_ || tp_ > 1 || n < kPrefillMinRows) {
+    if (!stack_ || n < kPrefillMinRows) {
         for (int i = 0; i < n; ++i) FB_RC(forward(tokens[i], length_, i == n - 1 ? logits_out : nullptr, s));
         return 0;
     }
@@ -993,7 +998,10 @@ int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaSt
         const int mp = (m + kPrefillBM - 1) / kPrefillBM * kPrefillBM;
         FB_CK(cudaMemcpyAsync(pf_tok_, tokens + done, size_t(m) * 4, cudaMemcpyHostToDevice, s));
         FB_RC(prefill_chunk(m, mp, length_, s));
-        FB_CK(cudaStreamSynchronize(s));  // the token buffer is reused by the next chunk
+        // the token buffer is reused by the next chunk; under tensor parallelism the wait
+        // has the host deadline (the chunk holds collectives)
+        FB_CK(cudaEventRecord(steps_done_, s));
+        FB_RC(wait_event(steps_done_));
         length_ += m;
         done += m;
         last_m = m;
@@ -1024,11 +1032,15 @@ int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaSt
         h.K = d_.hidden;
         FB_CK(dense_gemv_launch(h, head_kind_ == 1, sms_, s, false));
     }
+    // vocab-sharded head: every rank gets the full logits
+    if (tp_ > 1 && nccl().AllGather(logits_, logits_full_, size_t(v_), kNcclFloat32, comm_, s) != 0)
+        return FIRE_B200_ERR_STATE;
     if (logits_out != nullptr && logits_out != logits())
         FB_CK(cudaMemcpyAsync(logits_out, logits(), size_t(d_.vocab) * 4, cudaMemcpyDeviceToDevice, s));
+    FB_CK(cudaEventRecord(steps_done_, s));
+    FB_RC(wait_event(steps_done_));  // with the host deadline under tensor parallelism
     int err = 0;
-    FB_CK(cudaMemcpyAsync(&err, pf_err_, 4, cudaMemcpyDeviceToHost, s));
-    FB_CK(cudaStreamSynchronize(s));
+    FB_CK(cudaMemcpy(&err, pf_err_, 4, cudaMemcpyDeviceToHost));
     return err == 0 ? 0 : FIRE_B200_ERR_STATE;
 }
 

@@ -85,9 +85,11 @@ class Qwen3Engine {
     int generate_host(const int32_t* prompt, int n_prompt, int steps, int32_t* out_host, cudaStream_t s);
     // Batched prefill: consume n prompt tokens (host ids) at positions length()..,
     // leaving the KV cache and the last token's logits as n forward() calls would, with
-    // the projections on the tensor cores (BF16 operands, x as two BF16 terms). Falls back
-    // to forward() per token at tensor-parallel size > 1, with the per-op kernels, or for
-    // fewer than 64 tokens. Synchronises with `s` at the end (the host token copy).
+    // the projections on the tensor cores (BF16 operands, x as two BF16 terms). Under
+    // tensor parallelism each rank multiplies its shards (column-parallel q/k/v and
+    // gate/up, row-parallel o and down, whose [rows, hidden] partial sums are all-reduced
+    // over NCCL) and the vocab-sharded head is all-gathered. Falls back to forward() per
+    // token with the per-op kernels or for fewer than 64 tokens. Synchronises with `s`.
     int prefill(const int32_t* tokens, int n, float* logits_out, cudaStream_t s);
     int reset();
     int truncate(int length);

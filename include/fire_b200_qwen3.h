@@ -123,10 +123,12 @@ int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m);
 /* Batched prefill (the reference prefills token by token, demo/qwen_chat.cpp:202-213):
  * consume n prompt ids (host memory) at positions length()..length()+n-1 and leave the KV
  * cache, the length and the last token's logits (engine buffer, and logits_out if not
- * NULL) as n calls of fire_b200_qwen3_forward would. On one GPU, with 64 or more tokens,
- * the projections run on the tensor cores in chunks of 512 rows (BF16 weights, x as two BF16
- * terms, FP32 accumulation), so the values match forward() to about 1e-3; otherwise it is
- * forward() per token. Synchronises with `stream` before returning. */
+ * NULL) as n calls of fire_b200_qwen3_forward would. With 64 or more tokens the projections
+ * run on the tensor cores in chunks of 512 rows (BF16 weights, x as two BF16 terms, FP32
+ * accumulation), so the values match forward() to about 1e-3; under tensor parallelism each
+ * rank multiplies its shards and the row-parallel o / down outputs are all-reduced over NCCL.
+ * Otherwise (fewer tokens, or the per-op kernels) it is forward() per token. Synchronises
+ * with `stream` before returning. */
 int fire_b200_qwen3_prefill(fire_b200_qwen3* m, const int32_t* tokens, int n, float* logits_out,
                             void* stream);
 
