@@ -16,8 +16,10 @@
 
 namespace {
 
-// the last fire_b200 status a shim saw (Fire's kernel signatures return void)
-thread_local int g_last_rc = FIRE_B200_OK;
+// the last fire_b200 status a shim saw (Fire's kernel signatures return void);
+// kNotCalled until a shim runs
+constexpr int kNotCalled = -1000;
+thread_local int g_last_rc = kNotCalled;
 
 // src/op/kernels/cuda/matmul_kernel.cu:280-314, replaced
 void matmul_quant_kernel_cu(const tensor::Tensor& in, const tensor::Tensor& qw, tensor::Tensor& out,
@@ -67,7 +69,7 @@ extern "C" {
 
 // Fire's LinearOp with an Int4GroupWise Parameter on GPU tensors viewing the caller's device
 // pointers: returns LinearOp::forward's StatusCode (0 = Success); *kernel_rc receives the
-// fire_b200 status the shim saw.
+// fire_b200 status the shim saw, or -1000 when no kernel was called.
 int boundary_linear_w4(const float* x, const uint8_t* qw, const float* s, const uint8_t* z, float* y, int rows,
                        int n, int k, int group, void* stream, int* kernel_rc) {
     op::LinearOp linear;
@@ -84,7 +86,7 @@ int boundary_linear_w4(const float* x, const uint8_t* qw, const float* s, const 
     op::OpContext ctx;
     ctx._device_type = base::DeviceType::GPU;
     ctx._stream = static_cast<cudaStream_t>(stream);
-    g_last_rc = FIRE_B200_OK;
+    g_last_rc = kNotCalled;
     const base::Status st = linear.forward(in, out, ctx);
     if (kernel_rc) *kernel_rc = g_last_rc;
     return static_cast<int>(st.code());
@@ -101,7 +103,7 @@ int boundary_linear_dense(const float* x, const void* w, int bf16, float scale, 
     op::OpContext ctx;
     ctx._device_type = base::DeviceType::GPU;
     ctx._stream = static_cast<cudaStream_t>(stream);
-    g_last_rc = FIRE_B200_OK;
+    g_last_rc = kNotCalled;
     const base::Status st = linear.forward(in, out, ctx);
     if (kernel_rc) *kernel_rc = g_last_rc;
     return static_cast<int>(st.code());

@@ -18,6 +18,7 @@ pytestmark = pytest.mark.gpu
 
 LIB = os.path.join(os.path.dirname(O.__file__), "_ref", "libfire_boundary.so")
 SUCCESS, INVALID_ARGUMENT = 0, 7  # base::StatusCode (include/Fire/base/base.h:41-49)
+NOT_CALLED = -1000  # kernel_rc when the operator never reached a kernel
 
 
 @pytest.fixture(scope="module")
@@ -43,7 +44,8 @@ def rel_l2(a, b):
 def run_w4(L, x, p, s, z, rows, n, k, group):
     y = torch.empty((rows, n), device="cuda")
     krc = C.c_int(-99)
-    st = L.boundary_linear_w4(dev(x).data_ptr(), dev(p).data_ptr(), dev(s).data_ptr(), dev(z).data_ptr(), y.data_ptr(),
+    d = [dev(a) for a in (x, p, s, z)]  # kept alive across the call
+    st = L.boundary_linear_w4(d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), d[3].data_ptr(), y.data_ptr(),
                               rows, n, k, group, None, C.byref(krc))
     torch.cuda.synchronize()
     return st, krc.value, y.cpu().numpy()
@@ -84,7 +86,7 @@ def test_fire_linear_op_rejects_before_the_kernel(boundary):
     s = np.ones((n, 2), np.float32)
     z = np.zeros((n, 2), np.uint8)
     st, krc, _ = run_w4(boundary, np.ones(k, np.float32), p, s, z, 1, n, k, 100)
-    assert st == INVALID_ARGUMENT and krc == -99
+    assert st == INVALID_ARGUMENT and krc == NOT_CALLED
 
 
 def test_fire_linear_op_bf16_head_with_scale(boundary):
@@ -95,8 +97,9 @@ def test_fire_linear_op_bf16_head_with_scale(boundary):
     x = rng.normal(0, 1, k).astype(np.float32)
     y = torch.empty(n, device="cuda")
     krc = C.c_int(-99)
-    st = boundary.boundary_linear_dense(dev(x).data_ptr(), dev(wb).data_ptr(), 1, 0.5, y.data_ptr(), 1, n, k, None,
+    dx, dw = dev(x), dev(wb)
+    st = boundary.boundary_linear_dense(dx.data_ptr(), dw.data_ptr(), 1, 0.5, y.data_ptr(), 1, n, k, None,
                                         C.byref(krc))
     torch.cuda.synchronize()
-    assert st == SUCCESS and krc == 0
+    assert st == SUCCESS and krc.value == 0
     assert rel_l2(y.cpu().numpy(), O.linear_bf16(x, wb, 0.5)) <= 1e-5

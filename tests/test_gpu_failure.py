@@ -5,10 +5,11 @@ logits. Every wait inside the persistent layer-stack kernel is bounded (0.2 s of
 when one runs out the kernel records code 3 in the device decode state and returns. The
 injected failure is a wait that cannot be met: with FIRE_B200_FAULT_STALL=1 at engine
 creation, layer 0's o phase waits for one CTA more than the grid has (a counter that nothing
-bumps), until the engine is reset. Under tensor parallelism a peer that stops answering is
-met by the host-side deadline of the synchronising calls, which aborts the communicator
-(ncclCommAbort) and returns FIRE_B200_ERR_TIMEOUT. The reference's transactional rule is
-kept: a failed step is reported and the sequence restarts clean after reset
+bumps), until the engine is reset. Under tensor parallelism the stalled rank makes the other
+rank's poll of its exchange words run out; both report the failure and recover after reset.
+(A peer that stops launching altogether leaves the other rank's NCCL collective waiting; the
+host deadline that aborts the communicator for that case is not exercised here.) The
+reference's transactional rule is kept: a failed step is reported and the sequence restarts clean after reset
 (src/model/kv_cache.cpp:76-83, include/Fire/model/model.h:37-44).
 """
 import os
@@ -76,103 +77,61 @@ def test_stack_wait_timeout_is_reported_then_reset_recovers(cuda, monkeypatch):
     eng.close()
 
 
-def _tp_rank(rank, world, nid, prof, w, q, mode, release):
+def _tp_rank(rank, world, nid, prof, w, q):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
-        if mode == "stall" and rank == 1:
+        if rank == 1:
             os.environ["FIRE_B200_FAULT_STALL"] = "1"
         torch.cuda.set_device(rank)
-        from fire_b200 import _native as NN
         from fire_b200.engine import Qwen3Engine
 
-        eng = Qwen3Engine(prof, w, tp_rank=rank, tp_size=world, nccl_id=nid, deadline_ms=3000)
+        eng = Qwen3Engine(prof, w, tp_rank=rank, tp_size=world, nccl_id=nid, deadline_ms=30000)
         os.environ.pop("FIRE_B200_FAULT_STALL", None)
         eng.prepare(64)
         out = {"kps": eng.kernels_per_step}
-        if mode == "stall":
-            eng.forward(PROMPT[0], 0)
-            out["code"] = eng.status()
-            eng.reset()
-            out["toks"] = eng.generate_host(PROMPT, STEPS).tolist()
-            out["code_after"] = eng.status()
-            eng.close()
-        else:  # "leave": rank 1 stops launching after one good step; rank 0 meets the deadline
-            eng.forward(PROMPT[0], 0)
-            out["code"] = eng.status()
-            if rank == 0:
-                eng.forward(PROMPT[1], 1)
-                try:
-                    eng.status()
-                    out["late"] = "no error"
-                except NN.FireB200Error as e:
-                    out["late"] = e.status
-                eng.close()
-                q.put((rank, out, None))
-                return
-            # rank 1: stays alive (its memory stays mapped) without launching, until the
-            # parent says rank 0 is done; then leaves the group without waiting for it
-            q.put((rank, out, None))
-            release.get(timeout=300)
-            eng.abort()
-            eng.close()
-            return
+        # both ranks launch every step: rank 1 stalls in its own bounded wait, rank 0's poll
+        # of rank 1's exchange words runs out; nobody waits on a peer that stopped launching
+        eng.forward(PROMPT[0], 0)
+        out["code"] = eng.status()
+        eng.reset()
+        out["toks"] = eng.generate_host(PROMPT, STEPS).tolist()
+        out["code_after"] = eng.status()
+        eng.close()
         q.put((rank, out, None))
     except Exception as e:  # reported to the parent
         q.put((rank, None, repr(e)))
 
 
-def _spawn(prof, w, mode, world=2):
-    from fire_b200.engine import nccl_unique_id
-
-    nid = nccl_unique_id()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    procs = []
-    release = ctx.Queue()
-    for r in range(world):
-        procs.append(ctx.Process(target=_tp_rank, args=(r, world, nid, prof, w, q, mode, release)))
-    for p in procs:
-        p.start()
-    return procs, q, release
-
-
 def test_tp2_peer_timeout_is_reported_on_both_ranks_then_reset_recovers(cuda):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    from fire_b200.engine import nccl_unique_id
+
     prof = STACK
     w = synth.generate(prof, "mixed", seed=11)
-    procs, q, _ = _spawn(prof, w, "stall")
-    res = {}
-    for _ in range(2):
-        rank, out, err = q.get(timeout=600)
-        assert err is None, f"rank {rank}: {err}"
-        res[rank] = out
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    nid = nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, nid, prof, w, q), daemon=True) for r in range(2)]
+    try:
+        for p in procs:
+            p.start()
+        res = {}
+        for _ in range(2):
+            rank, out, err = q.get(timeout=240)
+            assert err is None, f"rank {rank}: {err}"
+            res[rank] = out
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:  # no rank may outlive the test
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     want = oracle_greedy(prof, w, PROMPT, STEPS, 64)
     for r in (0, 1):
         assert res[r]["kps"] <= 5  # layer-stack path with the in-kernel exchange
         assert res[r]["code"] == 3, (r, res[r])  # rank 1 stalled, rank 0's exchange poll ran out
         assert res[r]["code_after"] == 0
         assert res[r]["toks"] == want, r
-
-
-def test_tp2_rank_that_stops_launching_meets_the_host_deadline(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    prof = STACK
-    w = synth.generate(prof, "mixed", seed=11)
-    procs, q, release = _spawn(prof, w, "leave")
-    res = {}
-    for _ in range(2):
-        rank, out, err = q.get(timeout=600)
-        assert err is None, f"rank {rank}: {err}"
-        res[rank] = out
-        if rank == 0:
-            release.put(1)
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    assert res[0]["code"] == 0 and res[1]["code"] == 0
-    assert res[0]["late"] == N.ERR_TIMEOUT, res[0]

@@ -80,19 +80,25 @@ def test_tp_decode_matches_oracle(cuda, prof, world, stacked):
     nid = nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, prof, w, q, stacked)) for r in range(world)]
-    for p in procs:
-        p.start()
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, prof, w, q, stacked), daemon=True) for r in range(world)]
     res = {}
-    for _ in range(world):
-        rank, logits, toks, kps, err = q.get(timeout=600)
-        assert err is None, f"rank {rank}: {err}"
-        res[rank] = (logits, toks)
-        # the layer stack runs the step in embedding, stack, head, argmax, rank select
-        assert (kps <= 5) == stacked, kps
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    try:
+        for p in procs:
+            p.start()
+        for _ in range(world):
+            rank, logits, toks, kps, err = q.get(timeout=300)
+            assert err is None, f"rank {rank}: {err}"
+            res[rank] = (logits, toks)
+            # the layer stack runs the step in embedding, stack, head, argmax, rank select
+            assert (kps <= 5) == stacked, kps
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:  # no rank may outlive the test
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     O.set_threads(os.cpu_count() or 1)
     ref = O.Qwen3Oracle(prof, w, capacity=64)
     want_logits = [ref.forward(t, i) for i, t in enumerate(PROMPT)]
@@ -154,17 +160,24 @@ def test_tp_batched_prefill_matches_token_by_token(cuda, prof, world):
     nid = nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_prefill_rank, args=(r, world, nid, prof, w, prompt, q)) for r in range(world)]
-    for p in procs:
-        p.start()
+    procs = [ctx.Process(target=_prefill_rank, args=(r, world, nid, prof, w, prompt, q), daemon=True)
+             for r in range(world)]
     res = {}
-    for _ in range(world):
-        rank, got, got2, length, err = q.get(timeout=600)
-        assert err is None, f"rank {rank}: {err}"
-        res[rank] = (got, got2, length)
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    try:
+        for p in procs:
+            p.start()
+        for _ in range(world):
+            rank, got, got2, length, err = q.get(timeout=300)
+            assert err is None, f"rank {rank}: {err}"
+            res[rank] = (got, got2, length)
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:  # no rank may outlive the test
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     O.set_threads(os.cpu_count() or 1)
     ref = O.Qwen3Oracle(prof, w, capacity=n + 8)
     for i, t in enumerate(prompt):
