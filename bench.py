@@ -73,6 +73,8 @@ def parse():
     ap.add_argument("--gemv-shape", default=None,
                     help="with --gemv: only this shape (q, k, v, o, gate, up, down, qkv_fused, gate_up_fused, "
                          "lm_head), to size an ncu capture")
+    ap.add_argument("--trace-phases", action="store_true",
+                    help="only the per-phase timeline of one layer-stack launch at position 1791 (GPU timer)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers (0 = the model's 36); fewer only to size an ncu capture")
     return ap.parse_args()
@@ -552,6 +554,66 @@ def parity_leg(eng, p, wn, pos0, first, gpu_tokens, world, rank, logit_steps: in
     return parity, cpu_n / cpu_s, cpu_n
 
 
+PHASES = ("qkv", "attention", "o", "gate_up", "down")
+
+
+def trace_phases(layers: int = 0):
+    """Per-phase timeline of one Qwen3-8B layer-stack launch at position 1791 (random FP32
+    KV prefix imported into the engine), from the kernel's %globaltimer trace
+    (FIRE_B200_STACK_TRACE=1): per phase, averaged over layers 1..L-2, the time from the
+    previous phase's last CTA finishing to this phase's last CTA finishing, split into the
+    dependency wait (until the last CTA saw its input ready) and the input staging (median
+    CTA), next to the phase's bytes at the measured HBM peak."""
+    import dataclasses
+
+    import torch
+
+    os.environ["FIRE_B200_STACK_TRACE"] = "1"
+    from fire_b200 import synth
+    from fire_b200.engine import Qwen3Engine
+    from fire_b200.profiles import QWEN3_8B
+
+    p = QWEN3_8B if not layers else dataclasses.replace(QWEN3_8B, num_layers=layers)
+    w = synth.generate_torch(p, "mixed", seed=0, device="cuda")
+    eng = Qwen3Engine(p, w)
+    del w
+    eng.prepare(CAPACITY)
+    pos0 = PROMPT - 1
+    kc = np.random.default_rng(1).standard_normal((p.num_layers, pos0, p.num_kv_heads, 128), dtype=np.float32)
+    eng.kv_import(kc, kc)
+    for _ in range(3):
+        eng.truncate(pos0)
+        eng.forward(5, pos0)
+    torch.cuda.synchronize()
+    tr = eng.stack_trace().astype(np.int64)  # [cta, layer, phase, slot]
+    L = tr.shape[1]
+    done = [[tr[:, l, ph, 3][tr[:, l, ph, 3] > 0] for ph in range(5)] for l in range(L)]
+    peak = float(peaks().get("hbm_gbs", 6650.0))
+    H, F, Q, KV = p.hidden_size, p.intermediate_size, p.q_dim, p.kv_dim
+    w4 = lambda n, k: n * k // 2 + n * (k // 128) * 5
+    phase_bytes = [w4(Q + 2 * KV, H), 2 * pos0 * KV * 4, w4(H, Q), w4(2 * F, H), w4(H, F)]
+    rows = []
+    for ph in range(5):
+        span, wait, stage = [], [], []
+        for l in range(1, L - 1):
+            prev_l, prev_ph = (l, ph - 1) if ph > 0 else (l - 1, 4)
+            prev_end = done[prev_l][prev_ph].max()
+            act = tr[:, l, ph, 3] > 0
+            span.append((done[l][ph].max() - prev_end) / 1e3)
+            wait.append((tr[act, l, ph, 1].max() - prev_end) / 1e3)
+            stage.append(float(np.median(tr[act, l, ph, 2] - tr[act, l, ph, 1])) / 1e3)
+        rows.append({"phase": PHASES[ph], "us": round(float(np.mean(span)), 2),
+                     "dependency_wait_us": round(float(np.mean(wait)), 2),
+                     "staging_us": round(float(np.mean(stage)), 2) if ph != 1 else None,
+                     "bytes": phase_bytes[ph], "byte_ideal_us": round(phase_bytes[ph] / (peak * 1e3), 2)})
+    total = (done[L - 1][4].max() - tr[:, 0, 0, 0][tr[:, 0, 0, 0] > 0].min()) / 1e3
+    eng.close()
+    return {"metric": "layer-stack per-phase timeline (Qwen3-8B, position 1791)", "phases": rows,
+            "layer_us": round(sum(r["us"] for r in rows), 2),
+            "layer_byte_ideal_us": round(sum(r["byte_ideal_us"] for r in rows), 2),
+            "launch_us": round(total, 1), "layers": L, "peak_gbs": peak}
+
+
 def layer_stack_bytes(p, world: int, pos: int) -> float:
     """Algorithmic HBM bytes of one layer-stack launch at position `pos`: per layer the
     INT4 q/k/v, o, gate/up and down matrices (0.5 B per weight, 4 B scale + 1 B zero point
@@ -750,6 +812,12 @@ def main():
         torch.cuda.set_device(0)
         print(json.dumps({"metric": "INT4 prefill GEMM TFLOP/s (M=512, Qwen3-8B projection shapes)",
                           **prefill_sweep()}), flush=True)
+        return 0
+    if args.trace_phases:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps(trace_phases(args.layers)), flush=True)
         return 0
     if args.gemv:
         import torch
