@@ -896,7 +896,9 @@ int Qwen3Engine::prefill_buffers() {
     if (prefill_arena_) return 0;
     const size_t C = kPrefillChunk, H = d_.hidden;
     const size_t qkv = size_t(q_ + 2 * kv_), maxk = std::max({size_t(H), size_t(q_), size_t(f_)});
-    const size_t maxw = std::max({qkv * H, size_t(H) * q_, size_t(2 * f_) * H, size_t(H) * f_}) * 2;
+    // BF16 copy of the largest matrix, used only by the two-pass form
+    const size_t maxw =
+        prefill_two_pass() ? std::max({qkv * H, size_t(H) * q_, size_t(2 * f_) * H, size_t(H) * f_}) * 2 : 256;
     pf_gemm_ws_bytes_ = prefill_gemm_workspace_bytes(kPrefillChunk, static_cast<int>(maxk));
     std::unique_ptr<DeviceArena> ar(new DeviceArena(device_));
     const size_t sizes[] = {C * 4, C * H * 4, C * H * 4, C * qkv * 4, C * q_ * 4, C * q_ * 4, C * H * 4,
@@ -924,9 +926,15 @@ int Qwen3Engine::prefill_buffers() {
     return 0;
 }
 
-// y[mp, n] = x[mp, k] . W^T for a layer-stack item matrix W (dequantised into BF16 first)
+// y[mp, n] = x[mp, k] . W^T for a layer-stack item matrix W, dequantised into shared memory
+// inside the GEMM (or, with FIRE_B200_PREFILL_TWO_PASS=1, into BF16 scratch first)
 int Qwen3Engine::prefill_linear(const float* x, const uint8_t* items, int n, int k, float* y, int mp,
                                 cudaStream_t s) {
+    if (!prefill_two_pass()) {
+        FB_CK(prefill_w4_fused_launch(x, items, nullptr, nullptr, true, y, mp, n, k, pf_gemm_ws_, pf_gemm_ws_bytes_,
+                                      pf_err_, s));
+        return 0;
+    }
     FB_CK(prefill_dequant_items_launch(items, n, k, pf_w_, s));
     FB_CK(prefill_gemm_launch(x, pf_w_, y, mp, n, k, pf_gemm_ws_, pf_gemm_ws_bytes_, pf_err_, s));
     return 0;

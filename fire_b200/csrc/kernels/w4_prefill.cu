@@ -7,8 +7,8 @@
 //      and M*K*8 bytes.
 //   2. a BF16 GEMM, Y = X . W^T, FP32 accumulation in tensor memory:
 //      * CTA tile 128 (M) x 128 (N), K in stages of 64 (one 128-byte swizzle row);
-//      * one thread streams the x_hi, x_lo and W tiles with TMA (128-byte swizzle, no
-//        multicast) into a 4-stage shared-memory ring, full/empty mbarriers per stage;
+//      * one thread streams the x_hi, x_lo and W tiles with TMA (128-byte swizzle, each
+//        CTA loading its own tiles) into a 4-stage shared-memory ring, full/empty mbarriers;
 //      * one thread issues tcgen05.mma.cta_group::1.kind::f16 (M128 N128 K16: x_hi.W and
 //        x_lo.W per 16 K, eight per stage) from shared-memory descriptors into a
 //        128-column FP32 TMEM accumulator and frees each stage with tcgen05.commit;
@@ -21,6 +21,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -212,6 +214,221 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------------
+// Fused form: W is dequantised into shared memory inside the pipeline instead of through
+// BF16 scratch in HBM. Eight more warps (the "dequant warps"; thread d <-> row n0 + (d & 127)
+// of the W tile, half d >> 7 of its 64 K of the stage) read 16 bytes of nibbles per stage
+// from the .fire rows or the layer-stack items, kPrefetch stages ahead in registers so the
+// loads' latency hides behind the MMAs, form w = s * (q - z) in FP32 and round it once to
+// BF16 exactly as dequant_w4_bf16_kernel does, and store four 16-byte chunks into the
+// stage's B tile in the 128-byte-swizzle layout TMA would have produced (16-byte chunk c of
+// row r at chunk c ^ (r & 7)). They publish the tile with a proxy fence (the MMA reads
+// shared memory through the async proxy) and one arrival per warp on the stage's full
+// barrier, next to the producer's transaction count for the two X tiles. Same products and
+// accumulation order as the two-pass form, so the results are bit-identical; per stage the
+// TMA moves 32 KB instead of 48 KB, and the separate dequantisation pass is gone.
+constexpr int kDequantWarps = 8;
+constexpr int kFusedThreads = 128 + 32 * kDequantWarps;  // warps 0-3 as above, then the dequant warps
+constexpr int kPrefetch = 3;                              // stages of nibbles in flight per thread
+
+template <bool kItems>
+struct W4Src {
+    const uint8_t* q;      // .fire qweight [N, K/2] or layer-stack items
+    const float* s;        // .fire scales [N, K/128] (rows form)
+    const uint8_t* z;      // .fire zero points [N, K/128] (rows form)
+    int K;
+    // half h (16 bytes, 32 weights) of this row's 64 K of stage kt, its scale and zero point
+    __device__ __forceinline__ void load(int n, int kt, int h, uint4& w, float& sc, float& zp) const {
+        if (kItems) {
+            const int t = n >> 4, r = n & 15, it = kt >> 2, gi = (kt >> 1) & 1, half = kt & 1;
+            const uint8_t* item = q + (static_cast<size_t>(t) * (K / 256) + it) * 2208;
+            w = __ldg(reinterpret_cast<const uint4*>(item) + (((r >> 3) * 2 + gi) * 32 + 4 * (r & 7) + 2 * half + h));
+            sc = __ldg(reinterpret_cast<const float*>(item + 2048) + r * 2 + gi);
+            zp = static_cast<float>(__ldg(item + 2176 + r * 2 + gi));
+        } else {
+            w = __ldg(reinterpret_cast<const uint4*>(q + static_cast<size_t>(n) * (K / 2) + kt * 32) + h);
+            const size_t g = static_cast<size_t>(n) * (K / 128) + (kt >> 1);
+            sc = __ldg(s + g);
+            zp = static_cast<float>(__ldg(z + g));
+        }
+    }
+};
+
+template <bool kItems>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    prefill_w4_fused_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_alo,
+                            const W4Src<kItems> src, float* y, int M, int N, int K, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* done = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* failed = reinterpret_cast<int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kPrefillBM, n0 = blockIdx.y * kPrefillBN;  // M tiles of one N tile run together
+    const int KT = K / kPrefillBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1 + kDequantWarps);  // producer (with the X bytes) + the dequant warps
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_alo)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp >= 4) {
+        // dequant warps: row n0 + (d & 127), half d >> 7, every stage
+        const int d = threadIdx.x - 128, r = d & 127, h = d >> 7, n = n0 + r;
+        uint4 w[kPrefetch];
+        float sc[kPrefetch], zp[kPrefetch];
+#pragma unroll
+        for (int i = 0; i < kPrefetch; ++i)
+            if (i < KT) src.load(n, i, h, w[i], sc[i], zp[i]);
+        uint8_t* const brow0 = smem + 2 * kTileA + r * 128;
+        for (int kt = 0; kt < KT; ++kt) {
+            const int s = kt % kStages;
+            const uint4 cw = w[0];
+            const float csc = sc[0], czp = zp[0];
+#pragma unroll
+            for (int i = 0; i + 1 < kPrefetch; ++i) {  // shift the prefetch window (register moves)
+                w[i] = w[i + 1];
+                sc[i] = sc[i + 1];
+                zp[i] = zp[i + 1];
+            }
+            if (kt + kPrefetch < KT) src.load(n, kt + kPrefetch, h, w[kPrefetch - 1], sc[kPrefetch - 1], zp[kPrefetch - 1]);
+            bool ok = true;
+            if (kt >= kStages) ok = mbar_wait(&empty[s], static_cast<unsigned>((kt / kStages - 1) & 1));
+            const bool all_ok = __all_sync(0xffffffffu, ok);
+            if (!all_ok && lane == 0) {
+                atomicExch(err, 3);
+                *reinterpret_cast<volatile int*>(failed) = 1;
+            }
+            if (!all_ok || *reinterpret_cast<volatile int*>(failed)) break;
+            // 32 weights = 4 chunks of 8 (k = 8c .. 8c+7 are bytes 4c .. 4c+3 of the half)
+            uint8_t* brow = brow0 + s * kStageBytes;
+            const uint32_t wd[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t v = wd[c];
+                uint32_t o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float lo = csc * (static_cast<float>((v >> (8 * j)) & 0xF) - czp);
+                    const float hi = csc * (static_cast<float>((v >> (8 * j + 4)) & 0xF) - czp);
+                    const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);  // .x = lower k
+                    o[j] = *reinterpret_cast<const uint32_t*>(&b);
+                }
+                *reinterpret_cast<uint4*>(brow + (((4 * h + c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+            // visible to the tensor core's (async proxy) reads, then one arrival per warp
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&full[s])) : "memory");
+        }
+    } else if (warp == 0 && lane == 0) {
+        // producer: the x_hi and x_lo tiles of rows m0.., K slice kt
+        int issued = 0;
+        for (int kt = 0; kt < KT; ++kt) {
+            const int s = kt % kStages;
+            if (kt >= kStages && !mbar_wait(&empty[s], static_cast<unsigned>((kt / kStages - 1) & 1))) {
+                atomicExch(err, 1);
+                *reinterpret_cast<volatile int*>(failed) = 1;
+                break;
+            }
+            if (*reinterpret_cast<volatile int*>(failed)) break;
+            uint8_t* a = smem + s * kStageBytes;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])),
+                         "r"(2 * kTileA)
+                         : "memory");
+            tma_load_2d(a, &tma_a, kt * kPrefillBK, m0, &full[s]);
+            tma_load_2d(a + kTileA, &tma_alo, kt * kPrefillBK, m0, &full[s]);
+            issued = kt + 1;
+        }
+        // drain: every issued X copy lands before the CTA may exit (bounded)
+        for (int kt = issued > kStages ? issued - kStages : 0; kt < issued; ++kt) {
+            const int s = kt % kStages;
+            const unsigned long long t0 = gtime();
+            for (int i = 0;; ++i) {
+                // the X bytes of stage kt are in once the barrier's transaction count is met;
+                // the phase itself may also wait for dequant arrivals that a failure skipped
+                if (mbar_try(&full[s], static_cast<unsigned>((kt / kStages) & 1))) break;
+                if ((i & 63) == 63 && gtime() - t0 > kWaitNs) break;
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer
+        for (int kt = 0; kt < KT; ++kt) {
+            const int s = kt % kStages;
+            if (!mbar_wait(&full[s], static_cast<unsigned>((kt / kStages) & 1))) {
+                atomicExch(err, 2);
+                *reinterpret_cast<volatile int*>(failed) = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a = su32(smem + s * kStageBytes), alo = a + kTileA, b = a + 2 * kTileA;
+#pragma unroll
+            for (int k = 0; k < kPrefillBK / 16; ++k) {
+                umma_bf16(tmem, desc_sw128(a + 32 * k), desc_sw128(b + 32 * k), (kt | k) != 0);
+                umma_bf16(tmem, desc_sw128(alo + 32 * k), desc_sw128(b + 32 * k), 1);
+            }
+            umma_commit(&empty[s]);
+        }
+        umma_commit(done);
+    }
+    __syncwarp();
+    if (warp < 4) {
+        const bool ok = mbar_wait(done, 0) && *reinterpret_cast<volatile int*>(failed) == 0;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (__all_sync(0xffffffffu, ok)) {
+            const int row = m0 + warp * 32 + lane;
+            float* dst = y + static_cast<size_t>(row) * N + n0;
+#pragma unroll 1
+            for (int c = 0; c < kPrefillBN / 32; ++c) {
+                uint32_t r[32];
+                const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(c * 32);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                      "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                      "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                      "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < M) {
+                    float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        d4[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
 // W (INT4 group 128) -> BF16 [N, K]: one thread per 8 weights (one 32-bit word of nibbles)
 __global__ void dequant_w4_bf16_kernel(const uint8_t* __restrict__ qw, const float* __restrict__ scales,
                                        const uint8_t* __restrict__ zeros, __nv_bfloat16* __restrict__ out, int N,
@@ -375,12 +592,56 @@ cudaError_t prefill_gemm_launch(const float* x, const void* w_bf16, float* y, in
     return cudaGetLastError();
 }
 
+bool prefill_two_pass() {
+    static const bool two = [] {
+        const char* v = std::getenv("FIRE_B200_PREFILL_TWO_PASS");
+        return v != nullptr && std::strcmp(v, "1") == 0;
+    }();
+    return two;
+}
+
+cudaError_t prefill_w4_fused_launch(const float* x, const uint8_t* w, const float* scales, const uint8_t* zeros,
+                                    bool items, float* y, int M, int N, int K, void* workspace,
+                                    size_t workspace_bytes, int* err, cudaStream_t s) {
+    if (!prefill_supported(M, N, K, 128) || workspace == nullptr || err == nullptr || w == nullptr)
+        return cudaErrorInvalidValue;
+    if (items ? K % 256 != 0 : (scales == nullptr || zeros == nullptr)) return cudaErrorInvalidValue;
+    if (workspace_bytes < prefill_gemm_workspace_bytes(M, K)) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(workspace) |
+         reinterpret_cast<uintptr_t>(w)) % 16)
+        return cudaErrorInvalidValue;
+    const size_t xbytes = align256(static_cast<size_t>(M) * K * 2);
+    __nv_bfloat16* xb = static_cast<__nv_bfloat16*>(workspace);
+    __nv_bfloat16* xl = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + xbytes);
+    const long long n8 = static_cast<long long>(M) * K / 8;
+    split_bf16_kernel<<<static_cast<int>(std::min<long long>((n8 + 255) / 256, 4096)), 256, 0, s>>>(x, xb, xl, n8);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    CUtensorMap ma, malo;
+    if (!make_map(&ma, xb, M, K, kPrefillBM) || !make_map(&malo, xl, M, K, kPrefillBM)) return cudaErrorNotSupported;
+    const dim3 grid(static_cast<unsigned>(M / kPrefillBM), static_cast<unsigned>(N / kPrefillBN));
+    if (items) {
+        auto kern = prefill_w4_fused_kernel<true>;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, kFusedThreads, kSmemBytes, s>>>(ma, malo, W4Src<true>{w, nullptr, nullptr, K}, y, M, N, K, err);
+    } else {
+        auto kern = prefill_w4_fused_kernel<false>;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, kFusedThreads, kSmemBytes, s>>>(ma, malo, W4Src<false>{w, scales, zeros, K}, y, M, N, K, err);
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t prefill_w4_launch(const float* x, const uint8_t* qw, const float* scales, const uint8_t* zeros, float* y,
                               int M, int N, int K, void* workspace, size_t workspace_bytes, int* err,
                               cudaStream_t s) {
     if (!prefill_supported(M, N, K, 128) || workspace == nullptr || err == nullptr) return cudaErrorInvalidValue;
     if (workspace_bytes < prefill_workspace_bytes(M, N, K)) return cudaErrorInvalidValue;
     const size_t gws = prefill_gemm_workspace_bytes(M, K);
+    if (!prefill_two_pass())
+        return prefill_w4_fused_launch(x, qw, scales, zeros, false, y, M, N, K, workspace, gws, err, s);
     void* wb = static_cast<char*>(workspace) + gws;
     cudaError_t e = prefill_dequant_rows_launch(qw, scales, zeros, N, K, wb, s);
     if (e != cudaSuccess) return e;

@@ -25,6 +25,14 @@ cudaError_t prefill_dequant_rows_launch(const uint8_t* qw, const float* scales, 
 cudaError_t prefill_dequant_items_launch(const uint8_t* items, int N, int K, void* w_bf16, cudaStream_t s);
 cudaError_t prefill_gemm_launch(const float* x, const void* w_bf16, float* y, int M, int N, int K, void* workspace,
                                 size_t workspace_bytes, int* err, cudaStream_t s);
+// One pass: W (INT4 .fire rows with scales and zero points, or layer-stack items when
+// `items`) dequantised into shared memory inside the GEMM pipeline; only X's hi/lo split
+// uses the workspace (prefill_gemm_workspace_bytes). Bit-identical to dequantise + GEMM.
+cudaError_t prefill_w4_fused_launch(const float* x, const uint8_t* w, const float* scales, const uint8_t* zeros,
+                                    bool items, float* y, int M, int N, int K, void* workspace,
+                                    size_t workspace_bytes, int* err, cudaStream_t s);
+// FIRE_B200_PREFILL_TWO_PASS=1 selects the two-pass form (BF16 scratch in HBM, then the GEMM)
+bool prefill_two_pass();
 cudaError_t prefill_w4_launch(const float* x, const uint8_t* qw, const float* scales, const uint8_t* zeros, float* y,
                               int M, int N, int K, void* workspace, size_t workspace_bytes, int* err,
                               cudaStream_t s);

@@ -141,3 +141,25 @@ def test_engine_prefill_short_prompt_is_forward_per_token(cuda):
     with pytest.raises(N.FireB200Error):
         a.prefill([TINY.vocab_size], la)  # bad id: rejected, nothing consumed
     assert a.length == len(prompt)
+
+
+def test_fused_dequant_gemm_bit_identical_to_two_pass(cuda, tmp_path):
+    """The default one-pass kernel (W dequantised into shared memory inside the GEMM) gives
+    the same bits as dequantising W to BF16 in HBM first and then running the GEMM: the
+    Linear at the 8B projection shapes and a whole engine prefill + one decode step."""
+    import os
+    import subprocess
+    import sys
+
+    from tests import prefill_two_pass_child as child
+
+    path = tmp_path / "two_pass.npz"
+    env = dict(os.environ, FIRE_B200_PREFILL_TWO_PASS="1")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    subprocess.run([sys.executable, "-m", "tests.prefill_two_pass_child", str(path)], env=env, cwd=root,
+                   check=True, timeout=600)
+    want = np.load(path)
+    got = child.compute()
+    assert set(got) == set(want.files)
+    for key, g in got.items():
+        assert np.array_equal(g.view(np.uint32), want[key].view(np.uint32)), key

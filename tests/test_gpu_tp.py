@@ -1,4 +1,4 @@
-"""Tensor-parallel decode on 2 (or 4) GPUs, one process per GPU, NCCL between them.
+"""Tensor-parallel decode and prefill on 2, 4 and 8 GPUs, one process per GPU, NCCL between them.
 
 Each rank builds the engine with its shard (column-parallel q/k/v and gate/up, row-parallel
 o/down, vocab-sharded head, KV heads by rank) and runs the same steps; the all-gathered
@@ -143,7 +143,8 @@ def _prefill_rank(rank, world, nid, prof, w, prompt, q):
         q.put((rank, None, None, None, repr(e)))
 
 
-@pytest.mark.parametrize("prof,world", [(STACK, 2), (STACK, 4), (Q8B, 2)], ids=["stack-tp2", "stack-tp4", "8b-tp2"])
+@pytest.mark.parametrize("prof,world", [(STACK, 2), (STACK, 4), (Q8B, 2), (Q8B, 4), (Q8B, 8)],
+                         ids=["stack-tp2", "stack-tp4", "8b-tp2", "8b-tp4", "8b-tp8"])
 def test_tp_batched_prefill_matches_token_by_token(cuda, prof, world):
     """Batched prefill under tensor parallelism (each rank's shards on the tensor cores,
     o / down partial sums all-reduced, head all-gathered) against the token-by-token oracle
