@@ -439,7 +439,7 @@ PREFILL_SHAPES = [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)]  # q
 
 def prefill_sweep(reps: int = 10):
     """The tensor-core INT4 prefill Linear (fire_b200_linear_w4_prefill) at M = 512 on every
-    Qwen3-8B projection shape, timed with CUDA events per call (dequant + split + GEMM)."""
+    Qwen3-8B projection shape, timed with CUDA events per call (x conversion + GEMM)."""
     import torch
 
     from fire_b200 import _native as N
@@ -480,8 +480,14 @@ def prefill_sweep(reps: int = 10):
         tot_us += us
         out.append({"n": n, "k": k, "us": round(us, 1), "tflops": round(fl / us / 1e6, 1)})
         del x, q, s, z, y, ws
-    return {"m": PREFILL_M, "shapes": out, "sweep_tflops": round(tot_fl / tot_us / 1e6, 1),
-            "note": "per call: W dequant to BF16 + x hi/lo split + tcgen05 GEMM (2 BF16 MMAs per K16)"}
+    peak = float(peaks().get("bf16_tflops", 1590.0))
+    sweep = tot_fl / tot_us / 1e6
+    return {"m": PREFILL_M, "shapes": out, "sweep_tflops": round(sweep, 1), "peak_tflops": peak,
+            "frac": round(sweep / peak, 3),
+            "note": "useful flops 2*M*N*K per call (INT4 W dequantised to FP16 scratch, x to FP16 with a "
+                    "power-of-two row scale, tcgen05 GEMM with one FP16 MMA per K16; "
+                    "FIRE_B200_PREFILL_FUSED=1 times the one-pass form); peak = "
+                    "MEASURED_PEAKS.json bf16_tflops (of measured; FP16 runs at the BF16 rate)"}
 
 
 def parity_leg(eng, p, wn, pos0, first, gpu_tokens, world, rank, logit_steps: int = 4):

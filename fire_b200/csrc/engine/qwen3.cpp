@@ -896,9 +896,9 @@ int Qwen3Engine::prefill_buffers() {
     if (prefill_arena_) return 0;
     const size_t C = kPrefillChunk, H = d_.hidden;
     const size_t qkv = size_t(q_ + 2 * kv_), maxk = std::max({size_t(H), size_t(q_), size_t(f_)});
-    // BF16 copy of the largest matrix, used only by the two-pass form
+    // FP16 copy of the largest matrix, used by the two-pass form
     const size_t maxw =
-        prefill_two_pass() ? std::max({qkv * H, size_t(H) * q_, size_t(2 * f_) * H, size_t(H) * f_}) * 2 : 256;
+        !prefill_one_pass() ? std::max({qkv * H, size_t(H) * q_, size_t(2 * f_) * H, size_t(H) * f_}) * 2 : 256;
     pf_gemm_ws_bytes_ = prefill_gemm_workspace_bytes(kPrefillChunk, static_cast<int>(maxk));
     std::unique_ptr<DeviceArena> ar(new DeviceArena(device_));
     const size_t sizes[] = {C * 4, C * H * 4, C * H * 4, C * qkv * 4, C * q_ * 4, C * q_ * 4, C * H * 4,
@@ -926,16 +926,17 @@ int Qwen3Engine::prefill_buffers() {
     return 0;
 }
 
-// y[mp, n] = x[mp, k] . W^T for a layer-stack item matrix W, dequantised into shared memory
-// inside the GEMM (or, with FIRE_B200_PREFILL_TWO_PASS=1, into BF16 scratch first)
+// y[mp, n] = x[mp, k] . W^T for a layer-stack item matrix W, dequantised into FP16 scratch
+// first (two-pass, the default) or, with FIRE_B200_PREFILL_FUSED=1, into shared memory
+// inside the GEMM
 int Qwen3Engine::prefill_linear(const float* x, const uint8_t* items, int n, int k, float* y, int mp,
                                 cudaStream_t s) {
-    if (!prefill_two_pass()) {
+    if (prefill_one_pass()) {
         FB_CK(prefill_w4_fused_launch(x, items, nullptr, nullptr, true, y, mp, n, k, pf_gemm_ws_, pf_gemm_ws_bytes_,
                                       pf_err_, s));
         return 0;
     }
-    FB_CK(prefill_dequant_items_launch(items, n, k, pf_w_, s));
+    FB_CK(prefill_dequant_items_launch(items, n, k, pf_w_, pf_err_, s));
     FB_CK(prefill_gemm_launch(x, pf_w_, y, mp, n, k, pf_gemm_ws_, pf_gemm_ws_bytes_, pf_err_, s));
     return 0;
 }
@@ -1049,6 +1050,7 @@ int Qwen3Engine::prefill(const int32_t* tokens, int n, float* logits_out, cudaSt
     FB_RC(wait_event(steps_done_));  // with the host deadline under tensor parallelism
     int err = 0;
     FB_CK(cudaMemcpy(&err, pf_err_, 4, cudaMemcpyDeviceToHost));
+    if (err == 4) return FIRE_B200_ERR_UNSUPPORTED;  // weights beyond the FP16 range of the GEMM
     return err == 0 ? 0 : FIRE_B200_ERR_STATE;
 }
 

@@ -206,7 +206,7 @@ class Qwen3Engine {
     float *pf_o_ = nullptr, *pf_gu_ = nullptr, *pf_act_ = nullptr;
     void* pf_gemm_ws_ = nullptr;
     size_t pf_gemm_ws_bytes_ = 0;
-    void* pf_w_ = nullptr;  // BF16 copy of the matrix being multiplied
+    void* pf_w_ = nullptr;  // FP16 copy of the matrix being multiplied (two-pass form)
     int* pf_err_ = nullptr;
     bool stack_trace_on_ = false;  // FIRE_B200_STACK_TRACE=1: record the per-phase timeline
     bool stall_on_ = false;        // FIRE_B200_FAULT_STALL=1 (tests): StackArgs::stall armed by prepare

@@ -71,12 +71,14 @@ int fire_b200_linear_w4(const float* x, const uint8_t* qweight, const float* sca
 /* INT4 group-128 Linear for many rows (prefill, M >= 128) on the tcgen05 tensor cores.
  * Replaces matmul_quant_int4_fp32_naive for rows > 1 (src/op/kernels/cuda/matmul_kernel.cu:
  * 202-227, dispatched from :280-314). Same arguments and meaning as fire_b200_linear_w4,
- * but the product is taken on BF16 tensor cores: each weight s * (q - z) rounded once to
- * BF16, x as the sum of two BF16 terms (x_hi + x_lo), FP32 accumulation. Requires rows % 128 == 0,
- * n % 128 == 0, k % 128 == 0, group_size == 128, 16-byte aligned x, y and workspace.
- * workspace: at least fire_b200_linear_w4_prefill_workspace_bytes(rows, n, k) bytes of
- * device memory (x_hi, x_lo and the dequantised BF16 weights). status_dev: optional device int that a bounded wait
- * sets non-zero if it gives up (NULL: a word inside the library). */
+ * but the product is taken on FP16 tensor cores: each weight s * (q - z) rounded once to
+ * FP16, each row of x scaled by a power of two (its largest |x| into [2^14, 2^15)) and
+ * rounded once to FP16, FP32 accumulation, the row scale undone exactly. Requires
+ * rows % 128 == 0, n % 128 == 0, k % 128 == 0, group_size == 128, 16-byte aligned x, y and
+ * workspace, 4-byte aligned qweight and scales. workspace: at least fire_b200_linear_w4_prefill_workspace_bytes(rows,
+ * n, k) bytes of device memory. status_dev: optional device int (NULL: a word inside the
+ * library) that the kernel sets non-zero: 1-3 if a bounded wait gives up, 4 if a group's
+ * weights can leave the FP16 range (|s| * max(z, 15 - z) > 65504). */
 size_t fire_b200_linear_w4_prefill_workspace_bytes(int rows, int n, int k);
 int fire_b200_linear_w4_prefill(const float* x, const uint8_t* qweight, const float* scales,
                                 const uint8_t* zero_points, float* y, int rows, int n, int k,

@@ -1,5 +1,5 @@
-"""Child process of test_gpu_prefill.py: the same prefill cases with the two-pass form
-selected (FIRE_B200_PREFILL_TWO_PASS=1 in the environment, read once per process), results
+"""Child process of test_gpu_prefill.py: the same prefill cases with the one-pass form
+selected (FIRE_B200_PREFILL_FUSED=1 in the environment, read once per process), results
 saved to the .npz path given as the only argument."""
 import sys
 

@@ -148,7 +148,7 @@ def _prefill_rank(rank, world, nid, prof, w, prompt, q):
 def test_tp_batched_prefill_matches_token_by_token(cuda, prof, world):
     """Batched prefill under tensor parallelism (each rank's shards on the tensor cores,
     o / down partial sums all-reduced, head all-gathered) against the token-by-token oracle
-    to BF16-GEMM accuracy: last logits rel-L2 <= 1e-2 with the same argmax, the next decode
+    to FP16-GEMM accuracy: last logits rel-L2 <= 1e-2 with the same argmax, the next decode
     step likewise, and every rank bit-equal."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
