@@ -368,7 +368,7 @@ def gemv_sweep(reps_min: int = 100, only=None):
         return {"shapes": out, "lm_head": head, "peak_gbs": peak}
     big = [r for r in out if r["bytes"] > 20e6]
     return {"shapes": out, "lm_head": head, "peak_gbs": peak,
-            "int4_large_shape_frac": round(sum(r["bytes"] for r in big) / sum(r["bytes"] / r["frac"] for r in big), 3),
+            "int4_large_shape_frac": round(sum(r["bytes"] for r in big) / (sum(r["us"] for r in big) * 1e3) / peak, 3),
             "why_not_higher": "each INT4 launch is one short burst per warp (1-2.6 row tiles of 16 KB or less): "
                               "~3-4 us of launch, x staging and tail per launch against 1.4-8.4 us of bytes; "
                               "the 1.24 GB BF16 head streams at the copy peak",

@@ -112,6 +112,8 @@ from fire_b200.engine import Qwen3Engine  # noqa: E402
 from fire_b200.profiles import TINY, Qwen3Profile  # noqa: E402
 
 SMALL = Qwen3Profile("small-qwen3", 4096, 4096, 512, 1536, 3, 8, 4, 128)
+# four q heads per KV head, as Qwen3-8B
+G4 = Qwen3Profile("g4-qwen3", 4096, 4096, 1024, 1536, 2, 8, 2, 128)
 
 
 def _oracle_prefix(O, p, w, prompt, cap):
@@ -122,7 +124,7 @@ def _oracle_prefix(O, p, w, prompt, cap):
     return ref, lg
 
 
-@pytest.mark.parametrize("profile,n", [(TINY, 200), (SMALL, 200), (TINY, 600)])
+@pytest.mark.parametrize("profile,n", [(TINY, 200), (SMALL, 200), (TINY, 600), (G4, 200), (G4, 600)])
 def test_engine_prefill_matches_token_by_token(cuda, profile, n):
     """Batched prefill leaves the last logits and the KV cache as the token-by-token oracle
     does, to FP16-GEMM accuracy: logits rel-L2 <= 1e-2 with the same argmax, and the next
