@@ -888,7 +888,7 @@ int Qwen3Engine::kv_import(int length, const float* key, const float* value, cud
 }
 
 namespace {
-constexpr int kPrefillChunk = 512;    // prompt rows per batched step
+constexpr int kPrefillChunk = 2048;   // prompt rows per batched step (one pass of W per layer up to here)
 constexpr int kPrefillMinRows = 64;   // below this the per-token path is as fast
 }  // namespace
 

@@ -124,8 +124,9 @@ int fire_b200_qwen3_kernels_per_step(const fire_b200_qwen3* m);
  * consume n prompt ids (host memory) at positions length()..length()+n-1 and leave the KV
  * cache, the length and the last token's logits (engine buffer, and logits_out if not
  * NULL) as n calls of fire_b200_qwen3_forward would. With 64 or more tokens the projections
- * run on the tensor cores in chunks of 512 rows (BF16 weights, x as two BF16 terms, FP32
- * accumulation), so the values match forward() to about 1e-3; under tensor parallelism each
+ * and the causal attention run on the tensor cores in chunks of up to 2048 rows (FP16
+ * operands with FP32 accumulation for the projections; FP16 q.K^T and BF16 P.V with an FP32
+ * softmax for attention), so the values match forward() to about 1e-3; under tensor parallelism each
  * rank multiplies its shards and the row-parallel o / down outputs are all-reduced over NCCL.
  * Otherwise (fewer tokens, or the per-op kernels) it is forward() per token. Synchronises
  * with `stream` before returning. */

@@ -124,7 +124,7 @@ def _oracle_prefix(O, p, w, prompt, cap):
     return ref, lg
 
 
-@pytest.mark.parametrize("profile,n", [(TINY, 200), (SMALL, 200), (TINY, 600), (G4, 200), (G4, 600)])
+@pytest.mark.parametrize("profile,n", [(TINY, 200), (SMALL, 200), (G4, 200), (G4, 1100), (TINY, 2100)])
 def test_engine_prefill_matches_token_by_token(cuda, profile, n):
     """Batched prefill leaves the last logits and the KV cache as the token-by-token oracle
     does, to FP16-GEMM accuracy: logits rel-L2 <= 1e-2 with the same argmax, and the next
