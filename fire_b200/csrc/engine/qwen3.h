@@ -85,7 +85,7 @@ class Qwen3Engine {
     int generate_host(const int32_t* prompt, int n_prompt, int steps, int32_t* out_host, cudaStream_t s);
     // Batched prefill: consume n prompt tokens (host ids) at positions length()..,
     // leaving the KV cache and the last token's logits as n forward() calls would, with
-    // the projections on the tensor cores (BF16 operands, x as two BF16 terms). Under
+    // the projections (FP16 operands) and the causal attention on the tensor cores. Under
     // tensor parallelism each rank multiplies its shards (column-parallel q/k/v and
     // gate/up, row-parallel o and down, whose [rows, hidden] partial sums are all-reduced
     // over NCCL) and the vocab-sharded head is all-gathered. Falls back to forward() per
